@@ -1,0 +1,54 @@
+// kvd_decode.cuh -- launch-side declarations shared by the decode translation
+// units (split-KV flash decode on CUDA cores, combine, generic fallback).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "kvdecode.h"
+
+namespace kvd {
+
+// Everything a decode kernel needs, passed by value.
+struct DecodeParams {
+    const float* Q;
+    const int8_t* K;
+    const int8_t* V;
+    const float* ks;
+    const float* vs;
+    float* out;
+    int B, Hq, Hkv, D, group;
+    int S;                       // dense length (seq_lens == nullptr)
+    const int32_t* seq_lens;     // device [B] or nullptr
+    const int32_t* tile_prefix;  // ragged: device [B+1] cumulative tiles (x Hq); else nullptr
+    int64_t kv_sb, kv_sh, sc_sb, sc_sh, q_sb, q_sh, o_sb, o_sh;
+    float qscale;                // softmax_scale * log2(e)
+    uint32_t flags;
+    int64_t n_tiles;             // dense: total tiles; ragged: read from tile_prefix[B]
+    int tiles_per_head;          // dense only
+    int grid;                    // persistent CTAs
+    float* partials;             // 2*grid records of D+4 floats (nullptr when grid == 1)
+};
+
+// Tokens per tile of the CUDA-core kernel for a head dimension.
+constexpr int tile_tokens(int D) { return D == 64 ? 256 : 128; }
+
+bool fast_path_ok(const kvd_decode_desc& d, const float* Q, const int8_t* K, const int8_t* V);
+
+// Per-device cached properties.
+int device_sm_count();
+
+// Launchers (return the launch status; add their launch count to *launches).
+cudaError_t launch_plan(const int32_t* seq_lens, int B, int Hq, int tok, int32_t* prefix,
+                        cudaStream_t st, int* launches);
+cudaError_t launch_splitkv(const DecodeParams& p, cudaStream_t st, int* launches);
+cudaError_t launch_generic(const kvd_decode_desc& d, const float* Q, const int8_t* K,
+                           const int8_t* V, const float* ks, const float* vs, float* out,
+                           void* ws, size_t ws_bytes, cudaStream_t st, int* launches);
+size_t generic_workspace_size(const kvd_decode_desc& d);
+cudaError_t launch_combine_parts(const float* parts, int num_parts, int64_t part_stride, int num_heads,
+                                 int head_dim, float* out, int64_t out_stride, uint32_t flags,
+                                 cudaStream_t st, int* launches);
+
+}  // namespace kvd

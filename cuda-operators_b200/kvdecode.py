@@ -1,0 +1,292 @@
+"""Python host side of libkvdecode_b200.so (ctypes over the C ABI in include/kvdecode.h).
+
+The reference (Murmurwkk/cuda-operators kv_cache/*.cu) is driven from host
+C++ through ``extern "C"`` entry points; this module exposes the same entry
+points with the same names and argument meaning (``solve``,
+``kv_int8_split_launch``, ``kv_int8_simple_launch``) plus the extended API
+(batched / GQA / ragged decode, quantise-on-append, row quantisation, LSE
+combine). Device memory comes from torch tensors; torch is only plumbing
+here -- every computation runs in the library's CUDA kernels. There is no
+CPU fallback: if the shared library is missing, loading raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import re
+import subprocess
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parent
+LIB_PATH = HERE / "libkvdecode_b200.so"
+HEADER = ROOT / "include" / "kvdecode.h"
+
+KVD_FLAG_PARTIAL_OUT = 1
+KVD_STATUS_OK = 0
+KVD_STATUS_WAIT_TIMEOUT = 1
+KVD_STATUS_CACHE_FULL = 2
+CUDA_ERROR_INVALID_VALUE = 1
+
+c_void_p = ctypes.c_void_p
+c_int = ctypes.c_int
+c_int32 = ctypes.c_int32
+c_int64 = ctypes.c_int64
+c_uint32 = ctypes.c_uint32
+c_size_t = ctypes.c_size_t
+c_float = ctypes.c_float
+
+
+class DecodeDesc(ctypes.Structure):
+    """Mirror of ``kvd_decode_desc``."""
+
+    _fields_ = [
+        ("batch", c_int32),
+        ("num_q_heads", c_int32),
+        ("num_kv_heads", c_int32),
+        ("head_dim", c_int32),
+        ("max_seq_len", c_int32),
+        ("flags", c_uint32),
+        ("seq_lens", c_void_p),
+        ("kv_stride_b", c_int64),
+        ("kv_stride_h", c_int64),
+        ("sc_stride_b", c_int64),
+        ("sc_stride_h", c_int64),
+        ("q_stride_b", c_int64),
+        ("q_stride_h", c_int64),
+        ("o_stride_b", c_int64),
+        ("o_stride_h", c_int64),
+        ("softmax_scale", c_float),
+    ]
+
+
+class AppendDesc(ctypes.Structure):
+    """Mirror of ``kvd_append_desc``."""
+
+    _fields_ = [
+        ("batch", c_int32),
+        ("num_kv_heads", c_int32),
+        ("head_dim", c_int32),
+        ("capacity", c_int32),
+        ("kv_stride_b", c_int64),
+        ("kv_stride_h", c_int64),
+        ("sc_stride_b", c_int64),
+        ("sc_stride_h", c_int64),
+        ("new_stride_b", c_int64),
+        ("new_stride_h", c_int64),
+    ]
+
+
+_SIGNATURES = {
+    "solve": (None, [c_void_p] * 6 + [c_int] * 3),
+    "kv_int8_split_launch": (c_int, [c_void_p] * 6 + [c_int] * 3 + [c_void_p, c_void_p]),
+    "kv_int8_simple_launch": (c_int, [c_void_p] * 6 + [c_int] * 3 + [c_void_p, c_void_p]),
+    "kvd_workspace_size": (c_size_t, [ctypes.POINTER(DecodeDesc)]),
+    "kvd_decode_launch": (c_int, [ctypes.POINTER(DecodeDesc)] + [c_void_p] * 7 + [c_size_t, c_void_p]),
+    "kvd_combine_launch": (c_int, [c_void_p, c_int, c_int64, c_int, c_int, c_void_p, c_int64, c_uint32, c_void_p]),
+    "kvd_append_int8_launch": (c_int, [ctypes.POINTER(AppendDesc)] + [c_void_p] * 7 + [c_void_p]),
+    "kvd_quantize_rows_launch": (c_int, [c_void_p, c_int64, c_int, c_int64, c_void_p, c_int64, c_void_p, c_void_p]),
+    "kvd_device_status": (c_int, [ctypes.POINTER(c_int32)]),
+    "kvd_last_launch_count": (c_int, []),
+    "kvd_abi_version": (c_int, []),
+    "kvd_error_string": (ctypes.c_char_p, [c_int]),
+}
+
+_lib = None
+
+
+def build(force: bool = False) -> Path:
+    """Compile libkvdecode_b200.so in place with nvcc (sm_100a)."""
+    if force or not LIB_PATH.exists():
+        subprocess.run(["make", "-C", str(HERE), "-j8"], check=True)
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    """Load the library (raises if it has not been built: there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing; build it with `make -C {HERE}`")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def header_functions() -> list[str]:
+    """Names of every function declared in include/kvdecode.h."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    names = re.findall(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b([A-Za-z_]\w*)\s*\([^;{]*\)\s*;", text, flags=re.M)
+    return sorted(set(names))
+
+
+class KvdError(RuntimeError):
+    def __init__(self, code: int, where: str):
+        self.code = code
+        msg = lib().kvd_error_string(code)
+        super().__init__(f"{where} failed: cuda error {code} ({msg.decode() if msg else '?'})")
+
+
+def _check(code: int, where: str) -> None:
+    if code != 0:
+        raise KvdError(code, where)
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        import torch
+
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+# ---------------------------------------------------------------- reference ABI
+def solve(Q, K_int8, V_int8, k_scale, v_scale, output, num_heads: int, seq_len: int, head_dim: int) -> None:
+    """``solve`` of kv_cache/*.cu: default stream, no synchronisation, no return value."""
+    lib().solve(_ptr(Q), _ptr(K_int8), _ptr(V_int8), _ptr(k_scale), _ptr(v_scale), _ptr(output),
+                num_heads, seq_len, head_dim)
+
+
+def kv_int8_split_launch(Q, K_int8, V_int8, k_scale, v_scale, output, num_heads, seq_len, head_dim, S,
+                         stream=None) -> int:
+    """Returns the cudaError_t code, like kv_cache/KV_int8_split_optimized.cu:268-292."""
+    return lib().kv_int8_split_launch(_ptr(Q), _ptr(K_int8), _ptr(V_int8), _ptr(k_scale), _ptr(v_scale),
+                                      _ptr(output), num_heads, seq_len, head_dim, _ptr(S), _stream(stream))
+
+
+def kv_int8_simple_launch(Q, K_int8, V_int8, k_scale, v_scale, output, num_heads, seq_len, head_dim, S,
+                          stream=None) -> int:
+    """Returns the cudaError_t code, like kv_cache/new_kvint8.cu:85-100."""
+    return lib().kv_int8_simple_launch(_ptr(Q), _ptr(K_int8), _ptr(V_int8), _ptr(k_scale), _ptr(v_scale),
+                                       _ptr(output), num_heads, seq_len, head_dim, _ptr(S), _stream(stream))
+
+
+# ----------------------------------------------------------------- extended API
+def make_desc(q, k, ks, out, seq_lens=None, max_seq_len: int | None = None, softmax_scale: float = 0.0,
+              partial: bool = False) -> DecodeDesc:
+    """Descriptor for q [B,Hq,D], k/v [B,Hkv,cap,D] int8, ks/vs [B,Hkv,cap], out [B,Hq,D or D+4]."""
+    B, Hq, D = q.shape
+    Bk, Hkv, cap, Dk = k.shape
+    if Bk != B or Dk != D or Hq % Hkv:
+        raise ValueError(f"shape mismatch q{tuple(q.shape)} k{tuple(k.shape)}")
+    if k.stride(3) != 1 or k.stride(2) != D or ks.stride(2) != 1 or q.stride(2) != 1 or out.stride(2) != 1:
+        raise ValueError("token rows must be contiguous (d stride 1, K/V token stride D, scale token stride 1)")
+    d = DecodeDesc()
+    d.batch, d.num_q_heads, d.num_kv_heads, d.head_dim = B, Hq, Hkv, D
+    d.max_seq_len = cap if max_seq_len is None else max_seq_len
+    d.flags = KVD_FLAG_PARTIAL_OUT if partial else 0
+    d.seq_lens = _ptr(seq_lens)
+    d.kv_stride_b, d.kv_stride_h = k.stride(0), k.stride(1)
+    d.sc_stride_b, d.sc_stride_h = ks.stride(0), ks.stride(1)
+    d.q_stride_b, d.q_stride_h = q.stride(0), q.stride(1)
+    d.o_stride_b, d.o_stride_h = out.stride(0), out.stride(1)
+    d.softmax_scale = softmax_scale
+    return d
+
+
+def workspace_size(desc: DecodeDesc) -> int:
+    return int(lib().kvd_workspace_size(ctypes.byref(desc)))
+
+
+def decode(q, k, v, ks, vs, out=None, seq_lens=None, softmax_scale: float = 0.0, partial: bool = False,
+           workspace=None, max_seq_len: int | None = None, stream=None):
+    """Split-KV INT8 decode attention; returns ``out`` ([B,Hq,D], or [B,Hq,D+4] records if partial)."""
+    import torch
+
+    B, Hq, D = q.shape
+    if out is None:
+        out = torch.empty((B, Hq, D + 4 if partial else D), dtype=torch.float32, device=q.device)
+    if v.stride() != k.stride() or vs.stride() != ks.stride():
+        raise ValueError("K/V and k_scale/v_scale must share strides")
+    desc = make_desc(q, k, ks, out, seq_lens, max_seq_len, softmax_scale, partial)
+    if workspace is None:
+        n = workspace_size(desc)
+        workspace = torch.empty(max(n, 1), dtype=torch.uint8, device=q.device)
+    rc = lib().kvd_decode_launch(ctypes.byref(desc), _ptr(q), _ptr(k), _ptr(v), _ptr(ks), _ptr(vs), _ptr(out),
+                                 _ptr(workspace), workspace.numel(), _stream(stream))
+    _check(rc, "kvd_decode_launch")
+    return out
+
+
+def combine(parts, out=None, partial: bool = False, stream=None):
+    """LSE-combine records ``parts`` [P, H, D+4] into out [H, D] (or [H, D+4] records)."""
+    import torch
+
+    P, H, R = parts.shape
+    D = R - 4
+    if out is None:
+        out = torch.empty((H, R if partial else D), dtype=torch.float32, device=parts.device)
+    rc = lib().kvd_combine_launch(_ptr(parts), P, parts.stride(0), H, D, _ptr(out), out.stride(0),
+                                  KVD_FLAG_PARTIAL_OUT if partial else 0, _stream(stream))
+    _check(rc, "kvd_combine_launch")
+    return out
+
+
+def append(k_new, v_new, K, V, ks, vs, seq_lens, stream=None) -> None:
+    """Quantise-on-append of one token per (b, h): k_new/v_new [B,Hkv,D] fp32 into the cache."""
+    B, H, D = k_new.shape
+    d = AppendDesc()
+    d.batch, d.num_kv_heads, d.head_dim, d.capacity = B, H, D, K.shape[2]
+    d.kv_stride_b, d.kv_stride_h = K.stride(0), K.stride(1)
+    d.sc_stride_b, d.sc_stride_h = ks.stride(0), ks.stride(1)
+    d.new_stride_b, d.new_stride_h = k_new.stride(0), k_new.stride(1)
+    if v_new.stride() != k_new.stride() or V.stride() != K.stride() or vs.stride() != ks.stride():
+        raise ValueError("K/V (and their scales, and the new rows) must share strides")
+    rc = lib().kvd_append_int8_launch(ctypes.byref(d), _ptr(k_new), _ptr(v_new), _ptr(K), _ptr(V), _ptr(ks),
+                                      _ptr(vs), _ptr(seq_lens), _stream(stream))
+    _check(rc, "kvd_append_int8_launch")
+
+
+def quantize_rows(x, codes=None, scales=None, stream=None):
+    """Quantise a 2-D fp32 tensor row by row; returns (codes int8 like x, scales [rows])."""
+    import torch
+
+    rows, dim = x.shape
+    if codes is None:
+        codes = torch.empty((rows, dim), dtype=torch.int8, device=x.device)
+    if scales is None:
+        scales = torch.empty((rows,), dtype=torch.float32, device=x.device)
+    rc = lib().kvd_quantize_rows_launch(_ptr(x), rows, dim, x.stride(0), _ptr(codes), codes.stride(0),
+                                        _ptr(scales), _stream(stream))
+    _check(rc, "kvd_quantize_rows_launch")
+    return codes, scales
+
+
+def device_status() -> int:
+    """Synchronise, then read and clear the device status word (KVD_STATUS_* bits)."""
+    v = c_int32(0)
+    _check(lib().kvd_device_status(ctypes.byref(v)), "kvd_device_status")
+    return int(v.value)
+
+
+def last_launch_count() -> int:
+    return int(lib().kvd_last_launch_count())
+
+
+def algorithmic_bytes(B: int, Hq: int, Hkv: int, D: int, lens) -> int:
+    """Bytes a decode step must move: each (b, kv head) reads its codes and two
+    scales per token once, plus the fp32 query and output rows."""
+    if isinstance(lens, int):
+        tokens = B * lens
+    else:
+        tokens = int(sum(int(x) for x in lens))
+    return tokens * Hkv * (2 * D + 8) + B * Hq * D * 4 * 2
+
+
+def default_softmax_scale(D: int) -> float:
+    return 1.0 / math.sqrt(D)

@@ -1,0 +1,161 @@
+/*
+ * kvdecode.h -- C ABI of libkvdecode_b200.so, a B200 (sm_100a) INT8 KV-cache
+ * decode-attention library.
+ *
+ * Drop-in for the extern "C" entry points of Murmurwkk/cuda-operators'
+ * kv_cache/ kernels. Plain pointers and sizes only; every pointer argument is
+ * a DEVICE pointer unless stated otherwise. Layout of the reference entry
+ * points (unchanged): Q [H][D] fp32, K/V [H][S][D] int8 codes, k_scale/v_scale
+ * [H][S] fp32 (one scale per token), output [H][D] fp32, where H folds batch
+ * and heads. Attention is out[h] = softmax_t((q_h . K[h,t]) * ks[h,t] / sqrt(D))
+ * applied to V[h,t] * vs[h,t].
+ *
+ * All launches are asynchronous on the given stream (the default stream for
+ * `solve`); the caller synchronises before reading results.
+ */
+#ifndef KVDECODE_H
+#define KVDECODE_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVD_ABI_VERSION 1
+
+/* ------------------------------------------------------------------------ */
+/* Reference-compatible entry points                                         */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces `solve` of kv_cache/KV_int8.cu:306-316,
+ * kv_cache/KV_int8_single_buffer.cu:260-270,
+ * kv_cache/KV_int8_split_optimized.cu:294-304 and kv_cache/new_kvint8.cu:102-104
+ * (identical signatures). Launches on the default stream and returns without
+ * synchronising. Null pointers or non-positive sizes print one line to stderr
+ * and return, as KV_int8_split_optimized.cu:306-324 does. Scratch for split
+ * partials is allocated stream-ordered (cudaMallocAsync/cudaFreeAsync on the
+ * default stream) instead of the reference's cudaMalloc/cudaFree per call. */
+void solve(const float* Q, const int8_t* K_int8, const int8_t* V_int8,
+           const float* k_scale, const float* v_scale, float* output,
+           int num_heads, int seq_len, int head_dim);
+
+/* Replaces kv_int8_split_launch, kv_cache/KV_int8_split_optimized.cu:268-292.
+ * S is caller-owned scratch of at least num_heads*seq_len floats (the
+ * reference's score buffer). This implementation keeps no score matrix; it
+ * uses S for split-KV partials and picks the split count so that they fit.
+ * Returns cudaErrorInvalidValue on a null pointer or a non-positive size
+ * (KV_int8_split_optimized.cu:272-273), else the launch status. */
+cudaError_t kv_int8_split_launch(const float* Q, const int8_t* K_int8, const int8_t* V_int8,
+                                 const float* k_scale, const float* v_scale, float* output,
+                                 int num_heads, int seq_len, int head_dim,
+                                 float* S, cudaStream_t stream);
+
+/* Replaces kv_int8_simple_launch, kv_cache/new_kvint8.cu:85-100. Same contract
+ * as kv_int8_split_launch (same kernels). */
+cudaError_t kv_int8_simple_launch(const float* Q, const int8_t* K_int8, const int8_t* V_int8,
+                                  const float* k_scale, const float* v_scale, float* output,
+                                  int num_heads, int seq_len, int head_dim,
+                                  float* S, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Extended API (no reference counterpart: batch, GQA, ragged, strides)      */
+/* ------------------------------------------------------------------------ */
+
+/* Decode flags. */
+#define KVD_FLAG_PARTIAL_OUT 1u  /* write (m, l, o) records instead of normalised output */
+
+/* A partial record (KVD_FLAG_PARTIAL_OUT output and kvd_combine_launch input)
+ * is KVD_PARTIAL_STRIDE(D) floats: [0] = m, the running max of
+ * score*log2(e); [1] = l = sum_t 2^(score_t*log2(e) - m); [2],[3] unused;
+ * [4 .. 4+D) = o = sum_t 2^(score_t*log2(e) - m) * v_t (not divided by l).
+ * An empty record has m = -inf, l = 0, o = 0. */
+#define KVD_PARTIAL_STRIDE(D) ((D) + 4)
+
+typedef struct kvd_decode_desc {
+    int32_t batch;          /* B >= 1 */
+    int32_t num_q_heads;    /* Hq >= 1 */
+    int32_t num_kv_heads;   /* Hkv >= 1, Hq % Hkv == 0; query head hq reads kv head hq/(Hq/Hkv) */
+    int32_t head_dim;       /* D >= 1 */
+    int32_t max_seq_len;    /* length of every sequence when seq_lens == NULL, else an upper bound */
+    uint32_t flags;         /* KVD_FLAG_* */
+    const int32_t* seq_lens;/* device [B] current lengths (0 allowed), or NULL */
+    /* Strides in elements. Tokens of one head are contiguous: token stride is
+     * D codes for K/V and 1 float for the scales. */
+    int64_t kv_stride_b, kv_stride_h;   /* K and V share strides */
+    int64_t sc_stride_b, sc_stride_h;   /* k_scale and v_scale share strides */
+    int64_t q_stride_b, q_stride_h;     /* Q [B][Hq][D] by default */
+    int64_t o_stride_b, o_stride_h;     /* output rows (or partial records) */
+    float softmax_scale;    /* <= 0 selects 1/sqrt(D) */
+} kvd_decode_desc;
+
+/* Bytes of workspace kvd_decode_launch needs for this descriptor on the
+ * current device (0 is possible). */
+size_t kvd_workspace_size(const kvd_decode_desc* desc);
+
+/* Split-KV flash decode. `workspace` may be smaller than kvd_workspace_size
+ * (fewer splits are used) or NULL with workspace_bytes == 0. Concurrent calls
+ * need separate workspaces. */
+cudaError_t kvd_decode_launch(const kvd_decode_desc* desc,
+                              const float* Q, const int8_t* K, const int8_t* V,
+                              const float* k_scale, const float* v_scale, float* out,
+                              void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Log-sum-exp combine of `num_parts` partial-record arrays, each [num_heads]
+ * records of KVD_PARTIAL_STRIDE(head_dim) floats, part p starting at
+ * parts + p*part_stride. Writes normalised rows out[h*out_stride + d], or
+ * combined records when flags has KVD_FLAG_PARTIAL_OUT. Used after gathering
+ * per-GPU partials of a sequence split across GPUs. */
+cudaError_t kvd_combine_launch(const float* parts, int num_parts, int64_t part_stride,
+                               int num_heads, int head_dim, float* out, int64_t out_stride,
+                               uint32_t flags, cudaStream_t stream);
+
+/* Quantise-on-append: for every (b, h), quantise the new fp32 K and V rows
+ * (k_new/v_new + b*new_stride_b + h*new_stride_h, D floats each) with the
+ * symmetric per-token INT8 rule (scale = max|x|/127 in IEEE fp32,
+ * code = clamp(round-half-even(x/scale), -127, 127); all-zero row -> scale 0,
+ * codes 0), write codes at token seq_lens[b] of the cache and its scale, then
+ * increment seq_lens[b]. A sequence already at `capacity` is left unchanged
+ * and the device status word records KVD_STATUS_CACHE_FULL. */
+typedef struct kvd_append_desc {
+    int32_t batch, num_kv_heads, head_dim, capacity;
+    int64_t kv_stride_b, kv_stride_h;   /* cache strides (elements) */
+    int64_t sc_stride_b, sc_stride_h;
+    int64_t new_stride_b, new_stride_h; /* k_new / v_new strides (floats) */
+} kvd_append_desc;
+
+cudaError_t kvd_append_int8_launch(const kvd_append_desc* desc,
+                                   const float* k_new, const float* v_new,
+                                   int8_t* K, int8_t* V, float* k_scale, float* v_scale,
+                                   int32_t* seq_lens, cudaStream_t stream);
+
+/* Quantise `rows` contiguous fp32 rows of `dim` values (row stride x_stride
+ * floats) to codes (row stride code_stride bytes) and one scale per row, with
+ * the same rule as kvd_append_int8_launch. */
+cudaError_t kvd_quantize_rows_launch(const float* x, int64_t rows, int dim, int64_t x_stride,
+                                     int8_t* codes, int64_t code_stride, float* scales,
+                                     cudaStream_t stream);
+
+/* Device status word: kernels record bounded-wait timeouts and cache overflow
+ * here instead of trapping. kvd_device_status synchronises the current device,
+ * reads the word, clears it and returns it through *status. */
+#define KVD_STATUS_OK 0
+#define KVD_STATUS_WAIT_TIMEOUT 1
+#define KVD_STATUS_CACHE_FULL 2
+cudaError_t kvd_device_status(int32_t* status);
+
+/* Number of kernel launches issued by the most recent kvd_decode_launch /
+ * kv_int8_*_launch / solve call on this host thread (for launch accounting). */
+int kvd_last_launch_count(void);
+
+int kvd_abi_version(void);
+
+/* cudaGetErrorString of the CUDA runtime linked into this library. */
+const char* kvd_error_string(int error);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVDECODE_H */
