@@ -223,27 +223,41 @@ def run_ours(args) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
 
     cfg = wl.CONFIGS[args.config]
-    case = wl.make_case(cfg, seed=args.seed + rank, device=str(dev))
-    B = cfg.batch
+    B = args.batch or cfg.batch
+    case = wl.make_case(cfg, seed=args.seed + rank, device=str(dev), batch=B)
     out = torch.empty((B, cfg.q_heads, cfg.head_dim), dtype=torch.float32, device=dev)
     lens0 = case.seq_lens.clone() if cfg.ragged else None
     lens_final = [n + 1 for n in case.lens_host] if cfg.append else case.lens_host
-    nbytes = wl.step_bytes(cfg, lens_final if cfg.ragged else None)
+    nbytes = wl.step_bytes(cfg, lens_final if cfg.ragged else None, batch=B)
     desc = kvd.make_desc(case.q, case.K, case.ks, out, case.seq_lens)
     ws = torch.empty(max(kvd.workspace_size(desc), 1), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
 
-    def step():
+    def step():  # launches on the current stream (a capture stream while a graph is recorded)
         if cfg.append:
             case.seq_lens.copy_(lens0)
-            kvd.append(case.k_new, case.v_new, case.K, case.V, case.ks, case.vs, case.seq_lens, stream)
-        kvd.decode(case.q, case.K, case.V, case.ks, case.vs, out=out, seq_lens=case.seq_lens,
-                   workspace=ws, stream=stream)
+            kvd.append(case.k_new, case.v_new, case.K, case.V, case.ks, case.vs, case.seq_lens)
+        kvd.decode(case.q, case.K, case.V, case.ks, case.vs, out=out, seq_lens=case.seq_lens, workspace=ws)
 
     step()
     launches_per_step = kvd.last_launch_count() + (1 if cfg.append else 0)
     for _ in range(args.warmup):
         step()
+
+    # Decode steps are replayed from a CUDA graph (G steps per graph) so that
+    # host launch overhead does not hide the device time of small configs.
+    G = 10 if args.steps % 10 == 0 and not args.no_graph else 1
+    if G > 1:
+        graph = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph):
+            for _ in range(G):
+                step()
+        torch.cuda.synchronize()
+        graph.replay()
+        run_steps = graph.replay
+    else:
+        run_steps = step
 
     def timed(fn, n):
         torch.cuda.synchronize()
@@ -265,7 +279,7 @@ def run_ours(args) -> None:
         return ms
 
     with ClockSampler(local) as clk:
-        ms = timed(step, args.steps)
+        ms = timed(run_steps, args.steps // G) / G
 
     # ---- end to end through the reference-facing C ABI with host buffers
     q_host = case.q.cpu().pin_memory()
@@ -316,6 +330,7 @@ def run_ours(args) -> None:
                 "h2d_bytes_per_step": int(q_host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4),
                 "call": "kv_int8_split_launch" if flat else "kvd_decode_launch"},
         "gpu_launches": launches_per_step * args.steps,
+        "launch": f"CUDA graph of {G} steps" if G > 1 else "direct launches",
     }
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         gbs, sec, kind, threads, sample = cpu_measure(cfg, args.cpu_heads, 3)
@@ -335,8 +350,10 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--seed", type=int, default=17)
+    ap.add_argument("--batch", type=int, default=0, help="per-GPU batch override (profiling small cases)")
     ap.add_argument("--cpu-heads", type=int, default=512, help="query heads in the CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch every step directly instead of from a CUDA graph")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

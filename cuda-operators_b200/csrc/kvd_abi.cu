@@ -71,7 +71,8 @@ extern "C" size_t kvd_workspace_size(const kvd_decode_desc* desc) {
     size_t fast = 0;
     if (d.head_dim == 64 || d.head_dim == 128)
         fast = fast_prefix_bytes(d) +
-               static_cast<size_t>(2) * device_sm_count() * (d.head_dim + 4) * sizeof(float);
+               static_cast<size_t>(2) * device_sm_count() * sk_ctas_per_sm(d.head_dim) * (d.head_dim + 4) *
+                   sizeof(float);
     const size_t gen = generic_workspace_size(d);
     return fast > gen ? fast : gen;
 }
@@ -113,8 +114,7 @@ extern "C" cudaError_t kvd_decode_launch(const kvd_decode_desc* desc, const floa
     p.qscale = scale * 1.4426950408889634f;  // scores in base-2 exponent units
     p.flags = d.flags;
 
-    const int sms = device_sm_count();
-    int64_t grid = sms;
+    int64_t grid = static_cast<int64_t>(device_sm_count()) * sk_ctas_per_sm(d.head_dim);  // persistent CTAs
     if (!d.seq_lens) {
         p.tiles_per_head = d.max_seq_len > 0 ? (d.max_seq_len + tok - 1) / tok : 1;
         p.n_tiles = static_cast<int64_t>(d.batch) * d.num_q_heads * p.tiles_per_head;
@@ -130,7 +130,7 @@ extern "C" cudaError_t kvd_decode_launch(const kvd_decode_desc* desc, const floa
     p.partials = grid > 1 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + pre) : nullptr;
 
     if (d.seq_lens) {
-        e = launch_plan(d.seq_lens, d.batch, d.num_q_heads, tok, static_cast<int32_t*>(workspace), stream,
+        e = launch_plan(d.seq_lens, d.batch, d.num_q_heads, tok, d.max_seq_len, static_cast<int32_t*>(workspace), stream,
                         &tl_launches);
         if (e != cudaSuccess) return e;
     }

@@ -31,8 +31,32 @@ struct DecodeParams {
     float* partials;             // 2*grid records of D+4 floats (nullptr when grid == 1)
 };
 
+// Shape of the CUDA-core split-KV kernel per head dimension: consumer warps
+// per CTA, ring stages, resident CTAs per SM. A lane group of D/16 lanes owns
+// 4 tokens of a tile, so a tile holds CW * (32 / (D/16)) * 4 tokens.
+#ifndef KVD_SK128_CW
+#define KVD_SK128_CW 8
+#endif
+#ifndef KVD_SK128_NS
+#define KVD_SK128_NS 3
+#endif
+#ifndef KVD_SK128_CTAS
+#define KVD_SK128_CTAS 2
+#endif
+#ifndef KVD_SK64_CW
+#define KVD_SK64_CW 4
+#endif
+#ifndef KVD_SK64_NS
+#define KVD_SK64_NS 3
+#endif
+#ifndef KVD_SK64_CTAS
+#define KVD_SK64_CTAS 2
+#endif
+
+constexpr int sk_consumer_warps(int D) { return D == 64 ? KVD_SK64_CW : KVD_SK128_CW; }
+constexpr int sk_ctas_per_sm(int D) { return D == 64 ? KVD_SK64_CTAS : KVD_SK128_CTAS; }
 // Tokens per tile of the CUDA-core kernel for a head dimension.
-constexpr int tile_tokens(int D) { return D == 64 ? 256 : 128; }
+constexpr int tile_tokens(int D) { return sk_consumer_warps(D) * (32 / (D / 16)) * 4; }
 
 bool fast_path_ok(const kvd_decode_desc& d, const float* Q, const int8_t* K, const int8_t* V);
 
@@ -40,7 +64,7 @@ bool fast_path_ok(const kvd_decode_desc& d, const float* Q, const int8_t* K, con
 int device_sm_count();
 
 // Launchers (return the launch status; add their launch count to *launches).
-cudaError_t launch_plan(const int32_t* seq_lens, int B, int Hq, int tok, int32_t* prefix,
+cudaError_t launch_plan(const int32_t* seq_lens, int B, int Hq, int tok, int cap, int32_t* prefix,
                         cudaStream_t st, int* launches);
 cudaError_t launch_splitkv(const DecodeParams& p, cudaStream_t st, int* launches);
 cudaError_t launch_generic(const kvd_decode_desc& d, const float* Q, const int8_t* K,

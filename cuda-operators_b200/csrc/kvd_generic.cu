@@ -39,7 +39,7 @@ __global__ void __launch_bounds__(kGenThreads) generic_decode_kernel(const GenPa
     const int split = blockIdx.y;
     const int b = static_cast<int>(u / p.Hq), hq = static_cast<int>(u % p.Hq);
     const int hk = hq / p.group;
-    const int len = p.seq_lens ? max(0, p.seq_lens[b]) : p.S;
+    const int len = p.seq_lens ? min(max(0, p.seq_lens[b]), p.S) : p.S;  // clamp to the capacity
     const int t_lo = min(len, split * p.span), t_hi = min(len, (split + 1) * p.span);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* q = p.Q + b * p.q_sb + static_cast<int64_t>(hq) * p.q_sh;

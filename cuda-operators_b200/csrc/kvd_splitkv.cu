@@ -16,11 +16,13 @@
 //
 // Inside a CTA: one producer warp issues 1-D bulk copies (TMA engine) of the K
 // tile, V tile, the two scale windows and, at segment starts, the query row
-// into a ring of NS stages guarded by full/empty mbarriers. Eight consumer
-// warps share each stage: a lane group of LPT lanes owns TPG=4 tokens of the
-// tile and 16 dims each. Codes are dequantised exactly in registers, QK and PV
-// use packed fp32x2 FMAs, each lane group keeps its own online-softmax state,
-// and group states are merged only at segment ends.
+// into a ring of NS stages guarded by full/empty mbarriers. CW consumer warps
+// share each stage: a lane group of LPT = D/16 lanes owns 4 tokens of the tile
+// and 16 dims each. Codes are dequantised exactly in registers, QK and PV use
+// packed fp32x2 FMAs, each lane group keeps its own online-softmax state, and
+// the states are merged (group -> warp by shuffles, warp -> CTA through shared
+// memory) only at segment ends. Several CTAs share an SM so that one CTA's
+// segment merge or barrier wait is covered by the others' streaming.
 #include <cstdio>
 
 #include "kvd_common.cuh"
@@ -33,11 +35,11 @@ struct SkCfg {
     static constexpr int DPL = 16;                 // dims per lane
     static constexpr int LPT = D / DPL;            // lanes per token: 8 (D=128) or 4 (D=64)
     static constexpr int GPW = 32 / LPT;           // lane groups per warp
-    static constexpr int CW = 8;                   // consumer warps
+    static constexpr int CW = sk_consumer_warps(D);
+    static constexpr int NS = D == 64 ? KVD_SK64_NS : KVD_SK128_NS;
+    static constexpr int MINB = sk_ctas_per_sm(D);
     static constexpr int TPG = 4;                  // tokens per group per tile
-    static constexpr int NG = CW * GPW;            // groups per CTA
-    static constexpr int TOK = NG * TPG;           // tokens per tile
-    static constexpr int NS = 6;                   // ring stages
+    static constexpr int TOK = CW * GPW * TPG;     // tokens per tile
     static constexpr int THREADS = (CW + 1) * 32;  // + producer warp
     static constexpr int KV_BYTES = TOK * D;
     static constexpr int SC_FLOATS = TOK + 4;      // 16-byte aligned superset window
@@ -47,14 +49,16 @@ struct SkCfg {
     static constexpr int OFF_VS = OFF_KS + SC_FLOATS * 4;
     static constexpr int OFF_Q = OFF_VS + SC_FLOATS * 4;
     static constexpr int STAGE_BYTES = OFF_Q + D * 4;
-    static constexpr int MERGE_FLOATS = NG * (D + 2) + NG;  // acc + (m,l) + factors
+    static constexpr int ROW_STRIDE = CW * GPW * D;  // bytes between a group's consecutive tokens
+    static constexpr int MERGE_FLOATS = CW * (D + 2);  // one (m, l, o[D]) state per consumer warp
     static constexpr int OFF_MERGE = NS * STAGE_BYTES;
-    static constexpr int OFF_META = OFF_MERGE + MERGE_FLOATS * 4;
+    static constexpr int OFF_META = OFF_MERGE + ((MERGE_FLOATS * 4 + 15) & ~15);
     static constexpr int OFF_BAR = OFF_META + NS * 16;
     static constexpr int SMEM_BYTES = OFF_BAR + (2 * NS + 2) * 8;
     static_assert(TOK == tile_tokens(D), "tile size mismatch");
     static_assert(STAGE_BYTES % 16 == 0 && OFF_MERGE % 16 == 0 && OFF_BAR % 8 == 0, "alignment");
-    static_assert(SMEM_BYTES <= 232448, "shared memory");
+    static_assert(SMEM_BYTES * MINB <= 232448, "shared memory");
+    static_assert(CW * 32 >= D, "the CTA merge gives one consumer thread per output dim");
 };
 
 struct TileLoc {
@@ -79,7 +83,7 @@ __device__ __forceinline__ TileLoc locate_tile(const DecodeParams& p, int64_t g)
             if (static_cast<int64_t>(__ldg(p.tile_prefix + mid)) <= g) lo = mid; else hi = mid;
         }
         L.b = lo;
-        L.len = __ldg(p.seq_lens + lo);
+        L.len = min(max(0, __ldg(p.seq_lens + lo)), p.S);  // lengths beyond the capacity are clamped
         L.nt = L.len > 0 ? (L.len + TOK - 1) / TOK : 1;
         const int64_t r = g - __ldg(p.tile_prefix + lo);
         L.hq = static_cast<int>(r / L.nt);
@@ -109,11 +113,12 @@ __device__ __forceinline__ void splitkv_producer(const DecodeParams& p, uint8_t*
     uint64_t* empty = full + C::NS;
     StageMeta* meta = reinterpret_cast<StageMeta*>(smem + C::OFF_META);
     const uint64_t pol = policy_evict_first();
+    int s = 0;
+    uint32_t round_par = 0;  // parity of (tile index / NS)
+    bool wrapped = false;
     int64_t issued = 0;
-    for (int64_t g = g_begin; g < g_end; ++g, ++issued) {
-        const int64_t k = g - g_begin;
-        const int s = static_cast<int>(k % C::NS);
-        if (k >= C::NS && !mbar_wait(&empty[s], static_cast<uint32_t>((k / C::NS - 1) & 1))) break;
+    for (int64_t g = g_begin; g < g_end; ++g) {
+        if (wrapped && !mbar_wait(&empty[s], round_par ^ 1u)) break;
         const TileLoc L = locate_tile<C::TOK>(p, g);
         const int hk = L.hq / p.group;
         const int t0 = L.i * C::TOK;
@@ -163,6 +168,12 @@ __device__ __forceinline__ void splitkv_producer(const DecodeParams& p, uint8_t*
             const float* qp = p.Q + L.b * p.q_sb + static_cast<int64_t>(L.hq) * p.q_sh;
             bulk_g2s(st + C::OFF_Q, qp, qbytes, &full[s], pol);
         }
+        ++issued;
+        if (++s == C::NS) {
+            s = 0;
+            round_par ^= 1u;
+            wrapped = true;
+        }
     }
     // Never leave copies in flight into this CTA's shared memory: wait (bounded)
     // for the last stages issued.
@@ -171,34 +182,41 @@ __device__ __forceinline__ void splitkv_producer(const DecodeParams& p, uint8_t*
 }
 
 // ----------------------------------------------------------------- consumers
+// Lane roles (per consumer warp): lane group grp = lane / LPT owns tokens
+// row(t) = (t*CW + warp)*GPW + grp, t = 0..3, of every tile; lane li = lane % LPT
+// of the group owns dims [16*li, 16*li + 16). For QK a lane walks its four
+// tokens in the order t ^ r, r = the lane's token after the reduction, so the
+// transpose-reduce below needs no selects.
 template <int D>
 __device__ __forceinline__ void splitkv_consumer(const DecodeParams& p, uint8_t* smem,
                                                  int64_t g_begin, int64_t g_end) {
     using C = SkCfg<D>;
-    constexpr int LPT = C::LPT, GPW = C::GPW, CW = C::CW, NG = C::NG;
+    constexpr int LPT = C::LPT, GPW = C::GPW, CW = C::CW;
     constexpr int TB0 = LPT == 8 ? 2 : 1;  // lowest lane bit that selects the token after the reduce
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     uint64_t* empty = full + C::NS;
     uint64_t* mbar = empty + C::NS;
     const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + C::OFF_META);
     float* mrg_acc = reinterpret_cast<float*>(smem + C::OFF_MERGE);
-    float* mrg_ml = mrg_acc + NG * D;
+    float* mrg_ml = mrg_acc + CW * D;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = lane / LPT, li = lane % LPT;
-    const int gid = warp * GPW + grp;
-    const int tk = li / TB0;                       // token (of TPG) this lane scores
-    const int my_row = (tk * CW + warp) * GPW + grp;
+    const int r = (li / TB0) & 3;                              // token this lane scores
+    const int base = (warp * GPW + grp) * D + li * 16;        // byte offset of token 0's slice
+    const int my_row = (r * CW + warp) * GPW + grp;
+    int koff[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) koff[t] = C::OFF_K + base + (t ^ r) * C::ROW_STRIDE;
 
     float2 q2[8], acc[8];
     float m = -INFINITY, l = 0.f;
     bool seg_has_cta_first = true, seg_from_head_start = false;
-    uint32_t merge_idx = 0;
+    uint32_t merge_par = 0, ph = 0;
+    int s = 0;
 
     for (int64_t g = g_begin; g < g_end; ++g) {
-        const int64_t k = g - g_begin;
-        const int s = static_cast<int>(k % C::NS);
-        if (!mbar_wait(&full[s], static_cast<uint32_t>((k / C::NS) & 1))) return;
+        if (!mbar_wait(&full[s], ph)) return;
         const StageMeta mt = meta[s];
         const uint8_t* st = smem + s * C::STAGE_BYTES;
         if ((mt.flags & 1) || g == g_begin) {
@@ -217,12 +235,11 @@ __device__ __forceinline__ void splitkv_consumer(const DecodeParams& p, uint8_t*
             seg_from_head_start = (mt.flags & 1) != 0;
         }
 
-        // ---- QK: four tokens per lane group, 16 dims per lane.
+        // ---- QK partial dots over this lane's 16 dims, tokens in order t ^ r.
         float dk[4];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-            const int row = (t * CW + warp) * GPW + grp;
-            const uint4 w4 = *reinterpret_cast<const uint4*>(st + C::OFF_K + row * D + li * 16);
+            const uint4 w4 = *reinterpret_cast<const uint4*>(st + koff[t]);
             float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f), lo, hi;
             dequant4(w4.x, lo, hi); a = __ffma2_rn(q2[0], lo, a); b = __ffma2_rn(q2[1], hi, b);
             dequant4(w4.y, lo, hi); a = __ffma2_rn(q2[2], lo, a); b = __ffma2_rn(q2[3], hi, b);
@@ -231,26 +248,14 @@ __device__ __forceinline__ void splitkv_consumer(const DecodeParams& p, uint8_t*
             const float2 c = __fadd2_rn(a, b);
             dk[t] = c.x + c.y;
         }
-        // Transpose-reduce: after it, lane li holds the full dot of token tk.
-        float dot;
-        if constexpr (LPT == 8) {
-            const bool up = (li & 4) != 0;
-            const float s0 = up ? dk[0] : dk[2], s1 = up ? dk[1] : dk[3];
-            const float k0 = up ? dk[2] : dk[0], k1 = up ? dk[3] : dk[1];
-            const float e0 = k0 + __shfl_xor_sync(0xffffffffu, s0, 4);
-            const float e1 = k1 + __shfl_xor_sync(0xffffffffu, s1, 4);
-            const bool bit = (li & 2) != 0;
-            float f = (bit ? e1 : e0) + __shfl_xor_sync(0xffffffffu, bit ? e0 : e1, 2);
-            dot = f + __shfl_xor_sync(0xffffffffu, f, 1);
-        } else {
-            const bool up = (li & 2) != 0;
-            const float s0 = up ? dk[0] : dk[2], s1 = up ? dk[1] : dk[3];
-            const float k0 = up ? dk[2] : dk[0], k1 = up ? dk[3] : dk[1];
-            const float e0 = k0 + __shfl_xor_sync(0xffffffffu, s0, 2);
-            const float e1 = k1 + __shfl_xor_sync(0xffffffffu, s1, 2);
-            const bool bit = (li & 1) != 0;
-            dot = (bit ? e1 : e0) + __shfl_xor_sync(0xffffffffu, bit ? e0 : e1, 1);
-        }
+        // Transpose-reduce across the LPT lanes of the group; afterwards the
+        // lane holds the full dot of token r.
+        constexpr int X1 = LPT / 2, X2 = LPT / 4;
+        const float e0 = dk[0] + __shfl_xor_sync(0xffffffffu, dk[2], X1);
+        const float e1 = dk[1] + __shfl_xor_sync(0xffffffffu, dk[3], X1);
+        float dot = e0 + __shfl_xor_sync(0xffffffffu, e1, X2);
+        if constexpr (LPT == 8) dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+
         const float* ksm = reinterpret_cast<const float*>(st + C::OFF_KS);
         const float* vsm = reinterpret_cast<const float*>(st + C::OFF_VS);
         const bool valid = my_row < mt.n;
@@ -274,12 +279,12 @@ __device__ __forceinline__ void splitkv_consumer(const DecodeParams& p, uint8_t*
         const float wv = valid ? pr * vsm[(mt.offs >> 8) + my_row] : 0.f;
 
         // ---- PV
+        const uint8_t* vrow = st + C::OFF_V + base;
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
             const float w = __shfl_sync(0xffffffffu, wv, grp * LPT + t * TB0);
             const float2 w2 = make_float2(w, w);
-            const int row = (t * CW + warp) * GPW + grp;
-            const uint4 x4 = *reinterpret_cast<const uint4*>(st + C::OFF_V + row * D + li * 16);
+            const uint4 x4 = *reinterpret_cast<const uint4*>(vrow + t * C::ROW_STRIDE);
             float2 lo, hi;
             dequant4(x4.x, lo, hi); acc[0] = __ffma2_rn(w2, lo, acc[0]); acc[1] = __ffma2_rn(w2, hi, acc[1]);
             dequant4(x4.y, lo, hi); acc[2] = __ffma2_rn(w2, lo, acc[2]); acc[3] = __ffma2_rn(w2, hi, acc[3]);
@@ -288,38 +293,65 @@ __device__ __forceinline__ void splitkv_consumer(const DecodeParams& p, uint8_t*
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == C::NS) {
+            s = 0;
+            ph ^= 1u;
+        }
 
         if (!((mt.flags & 2) || g == g_end - 1)) continue;
 
-        // ---- segment end: merge the NG lane-group states.
+        // ---- segment end. 1) lane group: sum l over its lanes.
         float lg = l;
 #pragma unroll
         for (int o = 1; o < LPT; o <<= 1) lg += __shfl_xor_sync(0xffffffffu, lg, o);
         if (LPT == 8) lg *= 0.5f;  // each token was counted by two lanes
-        if (li == 0) {
-            mrg_ml[2 * gid] = m;
-            mrg_ml[2 * gid + 1] = lg;
-        }
-        float4* ag = reinterpret_cast<float4*>(mrg_acc + gid * D + li * 16);
+        // 2) warp: rescale the groups to the warp max and add them up.
+        float mw = m;
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-            ag[j] = make_float4(acc[2 * j].x, acc[2 * j].y, acc[2 * j + 1].x, acc[2 * j + 1].y);
+        for (int o = LPT; o < 32; o <<= 1) mw = fmaxf(mw, __shfl_xor_sync(0xffffffffu, mw, o));
+        const float f = m == -INFINITY ? 0.f : exp2f(m - mw);
+        lg *= f;
+        const float2 f2 = make_float2(f, f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = __fmul2_rn(acc[j], f2);
+#pragma unroll
+        for (int o = LPT; o < 32; o <<= 1) {
+            lg += __shfl_xor_sync(0xffffffffu, lg, o);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                acc[j].x += __shfl_xor_sync(0xffffffffu, acc[j].x, o);
+                acc[j].y += __shfl_xor_sync(0xffffffffu, acc[j].y, o);
+            }
+        }
+        if (grp == 0) {
+            float4* ag = reinterpret_cast<float4*>(mrg_acc + warp * D + li * 16);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                ag[j] = make_float4(acc[2 * j].x, acc[2 * j].y, acc[2 * j + 1].x, acc[2 * j + 1].y);
+            if (li == 0) {
+                mrg_ml[2 * warp] = mw;
+                mrg_ml[2 * warp + 1] = lg;
+            }
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&mbar[0]);
-        if (!mbar_wait(&mbar[0], merge_idx & 1)) return;
+        if (!mbar_wait(&mbar[0], merge_par)) return;
+        // 3) CTA: merge the CW warp states; thread d owns output dim d.
         const int ct = threadIdx.x;
         if (ct < D) {
             float M = -INFINITY;
-            for (int gg = 0; gg < NG; ++gg) M = fmaxf(M, mrg_ml[2 * gg]);
+#pragma unroll
+            for (int w = 0; w < CW; ++w) M = fmaxf(M, mrg_ml[2 * w]);
             float O = 0.f, Lsum = 0.f;
             if (M != -INFINITY) {
-                for (int gg = 0; gg < NG; ++gg) {
-                    const float f = exp2f(mrg_ml[2 * gg] - M);
-                    O = fmaf(f, mrg_acc[gg * D + ct], O);
-                    Lsum = fmaf(f, mrg_ml[2 * gg + 1], Lsum);
+#pragma unroll
+                for (int w = 0; w < CW; ++w) {
+                    const float fw = exp2f(mrg_ml[2 * w] - M);
+                    O = fmaf(fw, mrg_acc[w * D + ct], O);
+                    Lsum = fmaf(fw, mrg_ml[2 * w + 1], Lsum);
                 }
             }
-            const int b = mt.u / p.Hq, hq = mt.u - (mt.u / p.Hq) * p.Hq;
+            const int b = mt.u / p.Hq, hq = mt.u - b * p.Hq;
             if (seg_from_head_start && (mt.flags & 2)) {
                 float* row = p.out + b * p.o_sb + static_cast<int64_t>(hq) * p.o_sh;
                 if (p.flags & KVD_FLAG_PARTIAL_OUT) {
@@ -337,13 +369,13 @@ __device__ __forceinline__ void splitkv_consumer(const DecodeParams& p, uint8_t*
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&mbar[1]);
-        if (!mbar_wait(&mbar[1], merge_idx & 1)) return;
-        ++merge_idx;
+        if (!mbar_wait(&mbar[1], merge_par)) return;
+        merge_par ^= 1u;
     }
 }
 
 template <int D>
-__global__ void __launch_bounds__(SkCfg<D>::THREADS, 1) splitkv_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(SkCfg<D>::THREADS, SkCfg<D>::MINB) splitkv_kernel(const DecodeParams p) {
     using C = SkCfg<D>;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -425,7 +457,7 @@ __global__ void __launch_bounds__(128) splitkv_combine_kernel(const DecodeParams
 // -------------------------------------------------------------- ragged plan
 // prefix[0] = 0, prefix[b+1] = sum_{b' <= b} Hq * max(1, ceil(len_b'/tok)).
 __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* seq_lens, int B, int Hq, int tok,
-                                                    int32_t* prefix) {
+                                                    int cap, int32_t* prefix) {
     __shared__ int32_t warp_tot[32];
     __shared__ int32_t carry;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -435,7 +467,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* seq_lens, int
         const int b = base + tid;
         int v = 0;
         if (b < B) {
-            const int len = max(0, seq_lens[b]);
+            const int len = min(max(0, seq_lens[b]), cap);
             v = Hq * (len > 0 ? (len + tok - 1) / tok : 1);
         }
         int incl = v;
@@ -498,9 +530,9 @@ cudaError_t launch_splitkv(const DecodeParams& p, cudaStream_t st, int* launches
     return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_plan(const int32_t* seq_lens, int B, int Hq, int tok, int32_t* prefix,
+cudaError_t launch_plan(const int32_t* seq_lens, int B, int Hq, int tok, int cap, int32_t* prefix,
                         cudaStream_t st, int* launches) {
-    plan_kernel<<<1, 1024, 0, st>>>(seq_lens, B, Hq, tok, prefix);
+    plan_kernel<<<1, 1024, 0, st>>>(seq_lens, B, Hq, tok, cap, prefix);
     const cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) ++*launches;
     return e;

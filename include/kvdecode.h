@@ -68,10 +68,12 @@ cudaError_t kv_int8_simple_launch(const float* Q, const int8_t* K_int8, const in
 #define KVD_FLAG_PARTIAL_OUT 1u  /* write (m, l, o) records instead of normalised output */
 
 /* A partial record (KVD_FLAG_PARTIAL_OUT output and kvd_combine_launch input)
- * is KVD_PARTIAL_STRIDE(D) floats: [0] = m, the running max of
- * score*log2(e); [1] = l = sum_t 2^(score_t*log2(e) - m); [2],[3] unused;
- * [4 .. 4+D) = o = sum_t 2^(score_t*log2(e) - m) * v_t (not divided by l).
- * An empty record has m = -inf, l = 0, o = 0. */
+ * is KVD_PARTIAL_STRIDE(D) floats: [0] = m, a reference point in base-2
+ * exponent units (scores times log2(e)); it is at most the max and at least
+ * the max minus 8, because rescaling is lazy; [1] = l = sum_t 2^(s_t - m);
+ * [2],[3] unused; [4 .. 4+D) = o = sum_t 2^(s_t - m) * v_t (not divided by l).
+ * m + log2(l) is the base-2 log-sum-exp of the scores. An empty record has
+ * m = -inf, l = 0, o = 0. */
 #define KVD_PARTIAL_STRIDE(D) ((D) + 4)
 
 typedef struct kvd_decode_desc {
