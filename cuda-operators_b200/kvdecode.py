@@ -91,7 +91,10 @@ _SIGNATURES = {
     "kvd_last_launch_count": (c_int, []),
     "kvd_abi_version": (c_int, []),
     "kvd_error_string": (ctypes.c_char_p, [c_int]),
+    "kvd_decode_launch_noalloc": (c_int, [ctypes.POINTER(DecodeDesc)] + [c_void_p] * 6 + [c_void_p]),
 }
+
+NOALLOC_SCRATCH_BYTES = 512 * 1024
 
 _lib = None
 
@@ -220,6 +223,21 @@ def decode(q, k, v, ks, vs, out=None, seq_lens=None, softmax_scale: float = 0.0,
     rc = lib().kvd_decode_launch(ctypes.byref(desc), _ptr(q), _ptr(k), _ptr(v), _ptr(ks), _ptr(vs), _ptr(out),
                                  _ptr(workspace), workspace.numel(), _stream(stream))
     _check(rc, "kvd_decode_launch")
+    return out
+
+
+def decode_noalloc(q, k, v, ks, vs, out, seq_lens=None, softmax_scale: float = 0.0, partial: bool = False,
+                   max_seq_len: int | None = None, stream=None):
+    """Same decode for callers that may not allocate device memory: the
+    library's fixed scratch array replaces the workspace, so this allocates
+    nothing (``out`` must be given). Calls that overlap on the GPU race on that
+    array; the first call on a device should not be inside a stream capture."""
+    if v.stride() != k.stride() or vs.stride() != ks.stride():
+        raise ValueError("K/V and k_scale/v_scale must share strides")
+    desc = make_desc(q, k, ks, out, seq_lens, max_seq_len, softmax_scale, partial)
+    rc = lib().kvd_decode_launch_noalloc(ctypes.byref(desc), _ptr(q), _ptr(k), _ptr(v), _ptr(ks), _ptr(vs),
+                                         _ptr(out), _stream(stream))
+    _check(rc, "kvd_decode_launch_noalloc")
     return out
 
 

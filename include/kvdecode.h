@@ -105,6 +105,22 @@ cudaError_t kvd_decode_launch(const kvd_decode_desc* desc,
                               const float* k_scale, const float* v_scale, float* out,
                               void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* No counterpart in the reference. The same decode as kvd_decode_launch for
+ * callers that cannot allocate device memory when they decode (a framework that
+ * owns all device memory and gives a plugin only its inputs and outputs, or a
+ * serving loop that bans allocation on its hot path): its scratch lives in a
+ * fixed KVD_NOALLOC_SCRATCH_BYTES array inside the library, held by every GPU
+ * that loads the library until exit. Descriptors whose kvd_workspace_size()
+ * exceeds the array are rejected with cudaErrorInvalidValue. The first call on
+ * a device resolves the array's address (make it outside any stream capture).
+ * All calls share the array: calls that overlap on the GPU race. Allocates
+ * nothing. */
+#define KVD_NOALLOC_SCRATCH_BYTES (512u * 1024u)
+cudaError_t kvd_decode_launch_noalloc(const kvd_decode_desc* desc,
+                                      const float* Q, const int8_t* K, const int8_t* V,
+                                      const float* k_scale, const float* v_scale, float* out,
+                                      cudaStream_t stream);
+
 /* Log-sum-exp combine of `num_parts` partial-record arrays, each [num_heads]
  * records of KVD_PARTIAL_STRIDE(head_dim) floats, part p starting at
  * parts + p*part_stride. Writes normalised rows out[h*out_stride + d], or
