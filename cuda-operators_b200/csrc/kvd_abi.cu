@@ -74,7 +74,9 @@ extern "C" size_t kvd_workspace_size(const kvd_decode_desc* desc) {
                static_cast<size_t>(2) * device_sm_count() * sk_ctas_per_sm(d.head_dim) * (d.head_dim + 4) *
                    sizeof(float);
     const size_t gen = generic_workspace_size(d);
-    return fast > gen ? fast : gen;
+    const size_t gqa = d.num_q_heads > d.num_kv_heads && gqa_path_ok(d) ? gqa_workspace_size(d) : 0;
+    size_t need = fast > gen ? fast : gen;
+    return need > gqa ? need : gqa;
 }
 
 extern "C" cudaError_t kvd_decode_launch(const kvd_decode_desc* desc, const float* Q, const int8_t* K,
@@ -93,6 +95,10 @@ extern "C" cudaError_t kvd_decode_launch(const kvd_decode_desc* desc, const floa
     if (!fast_path_ok(d, Q, K, V))
         return launch_generic(d, Q, K, V, k_scale, v_scale, out, workspace, workspace_bytes, stream,
                               &tl_launches);
+
+    // Grouped-query heads share every K/V tile: tensor-core kernel.
+    if (d.num_q_heads > d.num_kv_heads && gqa_path_ok(d))
+        return launch_gqa_tc(d, Q, K, V, k_scale, v_scale, out, workspace, workspace_bytes, stream, &tl_launches);
 
     const int tok = tile_tokens(d.head_dim);
     const size_t pre = fast_prefix_bytes(d);

@@ -53,6 +53,14 @@ struct DecodeParams {
 #define KVD_SK64_CTAS 2
 #endif
 
+// Ring stages and resident CTAs per SM of the tcgen05 GQA kernel.
+#ifndef KVD_GQA_NS
+#define KVD_GQA_NS 2
+#endif
+#ifndef KVD_GQA_CTAS
+#define KVD_GQA_CTAS 2
+#endif
+
 constexpr int sk_consumer_warps(int D) { return D == 64 ? KVD_SK64_CW : KVD_SK128_CW; }
 constexpr int sk_ctas_per_sm(int D) { return D == 64 ? KVD_SK64_CTAS : KVD_SK128_CTAS; }
 // Tokens per tile of the CUDA-core kernel for a head dimension.
@@ -71,6 +79,14 @@ cudaError_t launch_generic(const kvd_decode_desc& d, const float* Q, const int8_
                            const int8_t* V, const float* ks, const float* vs, float* out,
                            void* ws, size_t ws_bytes, cudaStream_t st, int* launches);
 size_t generic_workspace_size(const kvd_decode_desc& d);
+cudaError_t launch_combine_records(const float* base, int nparts, int64_t part_stride, int64_t rec_stride,
+                                   int64_t rows, int rows_per_b, int D, float* out, int64_t o_sb, int64_t o_sh,
+                                   uint32_t flags, cudaStream_t st, int* launches);
+bool gqa_path_ok(const kvd_decode_desc& d);
+size_t gqa_workspace_size(const kvd_decode_desc& d);
+cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const float* Q, const int8_t* K, const int8_t* V,
+                          const float* ks, const float* vs, float* out, void* ws, size_t ws_bytes,
+                          cudaStream_t st, int* launches);
 cudaError_t launch_combine_parts(const float* parts, int num_parts, int64_t part_stride, int num_heads,
                                  int head_dim, float* out, int64_t out_stride, uint32_t flags,
                                  cudaStream_t st, int* launches);

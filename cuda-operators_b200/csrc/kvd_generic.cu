@@ -206,6 +206,16 @@ cudaError_t launch_generic(const kvd_decode_desc& d, const float* Q, const int8_
     return cudaSuccess;
 }
 
+cudaError_t launch_combine_records(const float* base, int nparts, int64_t part_stride, int64_t rec_stride,
+                                   int64_t rows, int rows_per_b, int D, float* out, int64_t o_sb, int64_t o_sh,
+                                   uint32_t flags, cudaStream_t st, int* launches) {
+    combine_records_kernel<<<static_cast<unsigned>(rows), 128, 0, st>>>(base, nparts, part_stride, rec_stride,
+                                                                         rows_per_b, D, out, o_sb, o_sh, flags);
+    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) ++*launches;
+    return e;
+}
+
 // Public combine for partials gathered from several GPUs: part k holds
 // num_heads records at parts + k*part_stride.
 cudaError_t launch_combine_parts(const float* parts, int num_parts, int64_t part_stride, int num_heads,

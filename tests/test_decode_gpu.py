@@ -155,6 +155,43 @@ def test_grouped_query_heads(Hq, Hkv):
     decode_checked(q, K, V, ks, vs)
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,S", [
+    (40, 64, 8, 300),    # 320 (b, kv head) items >= persistent CTAs: one item per group, no split
+    (4, 64, 8, 2048),    # config-5 group shape at small batch: split items + record combine
+    (2, 8, 4, 1000),     # group 2
+    (3, 16, 4, 513),     # group 4
+    (2, 32, 2, 700),     # group 16
+])
+def test_gqa_tensor_core_path(B, Hq, Hkv, S):
+    q, K, V, ks, vs = po.random_cache(B * Hq + S, B, Hq, Hkv, S, 128)
+    decode_checked(q, K, V, ks, vs)
+
+
+def test_gqa_ragged_and_records():
+    B, Hq, Hkv, cap, D = 5, 32, 4, 1500, 128
+    q, K, V, ks, vs = po.random_cache(55, B, Hq, Hkv, cap, D)
+    lens = np.array([1500, 0, 1, 129, 640], np.int32)
+    decode_checked(q, K, V, ks, vs, seq_lens=lens)
+    # partial records: combining one record set must reproduce the output
+    tq, tK, tV, tks, tvs = dev(q, K, V, ks, vs)
+    rec = kvd.decode(tq, tK, tV, tks, tvs, seq_lens=torch.tensor(lens, device=DEV), partial=True)
+    out = kvd.combine(rec.view(1, B * Hq, D + 4))
+    torch.cuda.synchronize()
+    assert_close(out.cpu().numpy().reshape(B, Hq, D), po.decode_f64(q, K, V, ks, vs, seq_lens=lens))
+
+
+def test_gqa_extreme_value_scales():
+    """Tiny and huge per-token scales and a dominant token: the fixed-point
+    exponents of the query and weight limbs must adapt per head and tile."""
+    B, Hq, Hkv, S, D = 2, 16, 2, 600, 128
+    q, K, V, ks, vs = po.random_cache(77, B, Hq, Hkv, S, D)
+    ks[0] *= np.float32(1e-3)
+    vs[1] *= np.float32(1e3)
+    ks[1, :, 17] *= np.float32(50.0)  # one token dominates the softmax of every head in batch 1
+    q[0, :3] *= np.float32(1e-4)
+    decode_checked(q, K, V, ks, vs)
+
+
 def test_partial_records_and_cross_split_combine():
     """Decode two token halves with KVD_FLAG_PARTIAL_OUT and merge them with
     kvd_combine_launch -- the single-GPU emulation of the sequence split
