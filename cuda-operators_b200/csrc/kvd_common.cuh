@@ -61,15 +61,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// As above, but lets the hardware suspend the warp for up to `hint_ns` until
+// the phase completes, instead of returning at once: a waiting warp then
+// spends no issue slots polling.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+constexpr uint32_t kSuspendHintNs = 1000000;  // 1 ms per suspended try
+
 // Bounded wait for the phase with the given parity to complete. Returns false
 // (and records KVD_STATUS_WAIT_TIMEOUT) if it has not completed within
 // kWaitTimeoutNs; the caller then stops issuing work and drains.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    for (uint32_t it = 0;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 63u) == 63u && globaltimer_ns() - t0 > kWaitTimeoutNs) {
+    for (;;) {
+        if (mbar_try_wait_suspend(bar, parity, kSuspendHintNs)) return true;
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
             record_status(KVD_STATUS_WAIT_TIMEOUT);
             return false;
         }

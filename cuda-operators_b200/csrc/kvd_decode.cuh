@@ -53,9 +53,12 @@ struct DecodeParams {
 #define KVD_SK64_CTAS 2
 #endif
 
-// Ring stages and resident CTAs per SM of the tcgen05 GQA kernel.
-#ifndef KVD_GQA_NS
-#define KVD_GQA_NS 2
+// K ring stages, V ring stages and resident CTAs per SM of the tcgen05 GQA kernel.
+#ifndef KVD_GQA_NK
+#define KVD_GQA_NK 3
+#endif
+#ifndef KVD_GQA_NV
+#define KVD_GQA_NV 2
 #endif
 #ifndef KVD_GQA_CTAS
 #define KVD_GQA_CTAS 2

@@ -23,9 +23,11 @@
 // fixed-point steps, whose absolute error is 2^-31 of the head's largest
 // query element and 2^-32 of the tile's largest weight.
 //
-// Roles (192 threads): warps 0-3 epilogue (TMEM lane quarter = warp), warp 4
-// TMA producer, warp 5 MMA issuer (also owns the TMEM allocation). Every wait
-// is bounded; on expiry the kernel records KVD_STATUS_WAIT_TIMEOUT and unwinds.
+// Roles: NWG epilogue warpgroups (warp w reads TMEM lane quarter w % 4; for
+// groups of 8 or 16 the heads are split between two warpgroups, which halves
+// the per-tile epilogue latency), then one TMA producer warp and one MMA
+// issuer warp (which also owns the TMEM allocation). Every wait is bounded; on
+// expiry the kernel records KVD_STATUS_WAIT_TIMEOUT and unwinds.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -50,36 +52,43 @@ struct GqaParams {
     uint32_t flags;
 };
 
-template <int G, int NS_>
+template <int G, int NK_, int NV_>
 struct GqaCfg {
     static constexpr int D = 128;
     static constexpr int TOK = 128;
-    static constexpr int NS = NS_;
+    static constexpr int NK = NK_;                                // K tile ring depth
+    static constexpr int NV = NV_;                                // V tile (+ scales) ring depth
     static constexpr int NP = (4 * G < 16) ? 16 : 4 * G;        // MMA N: limbs x heads, padded
     static constexpr int TMEM_COLS = (4 * NP <= 32) ? 32 : (4 * NP <= 64 ? 64 : (4 * NP <= 128 ? 128 : 256));
-    static constexpr int THREADS = 192;
+    static constexpr int NWG = G >= 8 ? 2 : 1;                  // epilogue warpgroups, heads split between them
+    static constexpr int HPW = G / NWG;                           // heads per warpgroup
+    static constexpr int CPW = NP / NWG;                          // MMA columns per warpgroup
+    static constexpr int THREADS = 32 * (4 * NWG + 2);
     static constexpr int SC_FLOATS = TOK + 4;
-    // stage: K tile | V tile | ks window | vs window, K/V 1024-byte aligned
-    static constexpr int OFF_K = 0;
-    static constexpr int OFF_V = 16384;
-    static constexpr int OFF_KS = 32768;
-    static constexpr int OFF_VS = OFF_KS + SC_FLOATS * 4;
-    static constexpr int STAGE_BYTES = ((OFF_VS + SC_FLOATS * 4) + 1023) & ~1023;
-    static constexpr int QB_BYTES = NP * 128;                    // K-major, 128-byte swizzle
-    static constexpr int WB_BYTES = TOK * NP;                    // MN-major, no swizzle
-    static constexpr int OFF_QB = NS * STAGE_BYTES;              // 2 buffers
-    static constexpr int OFF_WB = OFF_QB + 2 * QB_BYTES;         // 2 buffers
-    static constexpr int OFF_RED = OFF_WB + 2 * WB_BYTES;        // [2][4][32] floats
-    static constexpr int OFF_META = OFF_RED + 2 * 4 * 32 * 4;    // [NS] x 16 bytes
-    static constexpr int OFF_BAR = OFF_META + NS * 16;
-    // barriers: full[NS], empty[NS], then at 2*NS: s_full[2], s_free[2], w_full[2], o_full[2],
-    // o_free[2], q_full[2], red, done, drain
-    static constexpr int NBAR = 2 * NS + 15;
+    static constexpr int TILE_BYTES = TOK * D;                    // one K or V tile, 128-byte swizzle
+    static constexpr int SC_BYTES = 2 * SC_FLOATS * 4;            // ks and vs windows of one tile
+    static constexpr int OFF_KR = 0;                              // [NK] K tiles
+    static constexpr int OFF_VR = OFF_KR + NK * TILE_BYTES;       // [NV] V tiles
+    static constexpr int OFF_SC = OFF_VR + NV * TILE_BYTES;       // [NV] scale windows
+    static constexpr int QB_BYTES = NP * 128;                     // K-major, 128-byte swizzle
+    static constexpr int WB_BYTES = TOK * NP;                     // MN-major, no swizzle
+    static constexpr int OFF_QB = (OFF_SC + NV * SC_BYTES + 1023) & ~1023;  // 2 buffers
+    static constexpr int OFF_WB = OFF_QB + 2 * QB_BYTES;          // 2 buffers
+    static constexpr int OFF_RED = OFF_WB + 2 * WB_BYTES;         // [NWG][2][4][32] floats
+    static constexpr int OFF_META = OFF_RED + NWG * 2 * 4 * 32 * 4;  // [NV] x 16 bytes
+    static constexpr int OFF_BAR = OFF_META + NV * 16;
+    // barriers: kfull[NK], kempty[NK], vfull[NV], vempty[NV], s_full[2], s_free[2], w_full[2],
+    // o_full[2], o_free[2], q_full[2], red[NWG], done, drain
+    static constexpr int B_KFULL = 0, B_KEMPTY = NK, B_VFULL = 2 * NK, B_VEMPTY = 2 * NK + NV;
+    static constexpr int B_SFULL = 2 * NK + 2 * NV, B_SFREE = B_SFULL + 2, B_WFULL = B_SFREE + 2,
+                         B_OFULL = B_WFULL + 2, B_OFREE = B_OFULL + 2, B_QFULL = B_OFREE + 2, B_RED = B_QFULL + 2,
+                         B_DONE = B_RED + NWG, B_DRAIN = B_DONE + 1;
+    static constexpr int NBAR = B_DRAIN + 1;
     static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
     static constexpr int SMEM_USED = OFF_TMEM + 16;
-    static constexpr int SMEM_BYTES = SMEM_USED + 1024;          // slack to align the base to 1024
-    static_assert(G >= 1 && G <= 16, "group size");
-    static_assert(STAGE_BYTES % 1024 == 0 && OFF_QB % 1024 == 0 && QB_BYTES % 1024 == 0, "swizzle atoms");
+    static constexpr int SMEM_BYTES = SMEM_USED + 1024;           // slack to align the base to 1024
+    static_assert(G >= 1 && G <= 16 && G % NWG == 0 && CPW % 16 == 0, "group size");
+    static_assert(OFF_VR % 1024 == 0 && OFF_QB % 1024 == 0 && QB_BYTES % 1024 == 0, "swizzle atoms");
     static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
@@ -193,6 +202,18 @@ __device__ __forceinline__ float pow2i(int e) {  // 2^e for e in [-126, 127]
     return __int_as_float((e + 127) << 23);
 }
 
+// 2^x on the special-function unit (relative error about 2^-22; 2^-inf = 0).
+__device__ __forceinline__ float ex2_fast(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Smallest e with x < 2^e, for x >= 0 finite (subnormals and 0 give -126).
+__device__ __forceinline__ int exp_above(float x) {
+    return static_cast<int>((__float_as_uint(x) >> 23) & 0xFFu) - 126;
+}
+
 }  // namespace kvd
 
 namespace kvd {
@@ -220,12 +241,17 @@ struct __align__(16) GMeta {
 };
 
 // ------------------------------------------------------------------ producer
-template <int G, int NS>
+// Lane 0 streams K tiles, lane 1 streams V tiles with both scale windows and
+// the tile metadata; the two rings are released independently (K as soon as
+// QK has read it, V after PV and the softmax), so K loads run ahead of V.
+template <int G, int NK, int NV>
 __device__ __forceinline__ void gqa_producer(const CUtensorMap* kmap, const CUtensorMap* vmap, const GqaParams& p,
-                                             uint8_t* smem) {
-    using C = GqaCfg<G, NS>;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-    uint64_t* empty = full + NS;
+                                             uint8_t* smem, bool v_side) {
+    using C = GqaCfg<G, NK, NV>;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+    const int R = v_side ? NV : NK;
+    uint64_t* full = bars + (v_side ? C::B_VFULL : C::B_KFULL);
+    uint64_t* empty = bars + (v_side ? C::B_VEMPTY : C::B_KEMPTY);
     GMeta* meta = reinterpret_cast<GMeta*>(smem + C::OFF_META);
     const uint64_t pol = policy_evict_first();
     int s = 0;
@@ -238,58 +264,59 @@ __device__ __forceinline__ void gqa_producer(const CUtensorMap* kmap, const CUte
             if (wrapped && !mbar_wait(&empty[s], round_par ^ 1u)) { ok = false; break; }
             const int t0 = I.t_lo + tt * C::TOK;
             const int n = max(0, min(C::TOK, I.t_hi - t0));
-            uint8_t* st = smem + s * C::STAGE_BYTES;
-            uint32_t bytes = 0, kwin = 0, vwin = 0;
-            int koff = 0, voff = 0;
-            uintptr_t ka0 = 0, va0 = 0;
-            if (n > 0) {
-                const int64_t sc_off = I.b * p.sc_sb + I.hk * p.sc_sh + t0;
-                const uintptr_t ka = reinterpret_cast<uintptr_t>(p.ks + sc_off);
-                const uintptr_t va = reinterpret_cast<uintptr_t>(p.vs + sc_off);
-                ka0 = ka & ~uintptr_t(15);
-                va0 = va & ~uintptr_t(15);
-                koff = static_cast<int>((ka - ka0) >> 2);
-                voff = static_cast<int>((va - va0) >> 2);
-                kwin = static_cast<uint32_t>(((ka + 4u * n + 15u) & ~uintptr_t(15)) - ka0);
-                vwin = static_cast<uint32_t>(((va + 4u * n + 15u) & ~uintptr_t(15)) - va0);
-                bytes = 2u * 16384u + kwin + vwin;  // tensor boxes always deliver the whole box
-            }
-            GMeta mt;
-            mt.it = it;
-            mt.n = n;
-            mt.flags = (tt == 0 ? 1 : 0) | (tt == I.ntiles - 1 ? 2 : 0);
-            mt.offs = koff | (voff << 8);
-            meta[s] = mt;
-            mbar_arrive_expect_tx(&full[s], bytes);
-            if (n > 0) {
-                tma_load_4d(st + C::OFF_K, kmap, 0, t0, I.hk, I.b, &full[s], pol);
-                tma_load_4d(st + C::OFF_V, vmap, 0, t0, I.hk, I.b, &full[s], pol);
-                bulk_g2s(st + C::OFF_KS, reinterpret_cast<const void*>(ka0), kwin, &full[s], pol);
-                bulk_g2s(st + C::OFF_VS, reinterpret_cast<const void*>(va0), vwin, &full[s], pol);
+            if (!v_side) {
+                mbar_arrive_expect_tx(&full[s], n > 0 ? static_cast<uint32_t>(C::TILE_BYTES) : 0u);
+                if (n > 0) tma_load_4d(smem + C::OFF_KR + s * C::TILE_BYTES, kmap, 0, t0, I.hk, I.b, &full[s], pol);
+            } else {
+                uint32_t kwin = 0, vwin = 0;
+                int koff = 0, voff = 0;
+                uintptr_t ka0 = 0, va0 = 0;
+                if (n > 0) {
+                    const int64_t sc_off = I.b * p.sc_sb + I.hk * p.sc_sh + t0;
+                    const uintptr_t ka = reinterpret_cast<uintptr_t>(p.ks + sc_off);
+                    const uintptr_t va = reinterpret_cast<uintptr_t>(p.vs + sc_off);
+                    ka0 = ka & ~uintptr_t(15);
+                    va0 = va & ~uintptr_t(15);
+                    koff = static_cast<int>((ka - ka0) >> 2);
+                    voff = static_cast<int>((va - va0) >> 2);
+                    kwin = static_cast<uint32_t>(((ka + 4u * n + 15u) & ~uintptr_t(15)) - ka0);
+                    vwin = static_cast<uint32_t>(((va + 4u * n + 15u) & ~uintptr_t(15)) - va0);
+                }
+                GMeta mt;
+                mt.it = it;
+                mt.n = n;
+                mt.flags = (tt == 0 ? 1 : 0) | (tt == I.ntiles - 1 ? 2 : 0);
+                mt.offs = koff | (voff << 8);
+                meta[s] = mt;
+                mbar_arrive_expect_tx(&full[s], n > 0 ? static_cast<uint32_t>(C::TILE_BYTES) + kwin + vwin : 0u);
+                if (n > 0) {
+                    uint8_t* sc = smem + C::OFF_SC + s * C::SC_BYTES;
+                    tma_load_4d(smem + C::OFF_VR + s * C::TILE_BYTES, vmap, 0, t0, I.hk, I.b, &full[s], pol);
+                    bulk_g2s(sc, reinterpret_cast<const void*>(ka0), kwin, &full[s], pol);
+                    bulk_g2s(sc + C::SC_FLOATS * 4, reinterpret_cast<const void*>(va0), vwin, &full[s], pol);
+                }
             }
             ++issued;
-            if (++s == NS) { s = 0; round_par ^= 1u; wrapped = true; }
+            if (++s == R) { s = 0; round_par ^= 1u; wrapped = true; }
         }
     }
-    for (int64_t j = issued > NS ? issued - NS : 0; j < issued; ++j)
-        mbar_wait(&full[j % NS], static_cast<uint32_t>((j / NS) & 1));
+    for (int64_t j = issued > R ? issued - R : 0; j < issued; ++j)
+        mbar_wait(&full[j % R], static_cast<uint32_t>((j / R) & 1));
 }
 
 // ------------------------------------------------------------------ MMA issuer
-template <int G, int NS>
-__device__ __forceinline__ bool gqa_mma_pv(uint8_t* smem, uint32_t tmem, int64_t j, int sj) {
-    using C = GqaCfg<G, NS>;
+template <int G, int NK, int NV>
+__device__ __forceinline__ bool gqa_mma_pv(uint8_t* smem, uint32_t tmem, int64_t j) {
+    using C = GqaCfg<G, NK, NV>;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-    uint64_t* empty = bars + NS;
-    uint64_t* w_full = bars + 2 * NS + 4;
-    uint64_t* o_full = bars + 2 * NS + 6;
-    uint64_t* o_free = bars + 2 * NS + 8;
     const int bj = static_cast<int>(j & 1);
-    if (!mbar_wait(&w_full[bj], static_cast<uint32_t>((j >> 1) & 1))) return false;
-    if (j >= 2 && !mbar_wait(&o_free[bj], static_cast<uint32_t>(((j >> 1) - 1) & 1))) return false;
+    const int sv = static_cast<int>(j % NV);
+    if (!mbar_wait(&bars[C::B_VFULL + sv], static_cast<uint32_t>((j / NV) & 1))) return false;
+    if (!mbar_wait(&bars[C::B_WFULL + bj], static_cast<uint32_t>((j >> 1) & 1))) return false;
+    if (j >= 2 && !mbar_wait(&bars[C::B_OFREE + bj], static_cast<uint32_t>(((j >> 1) - 1) & 1))) return false;
     tc_fence_after();
     constexpr uint32_t idesc = idesc_i8(true, false, true, true, C::NP, 128);
-    const uint32_t vbase = smem_u32(smem + sj * C::STAGE_BYTES + C::OFF_V);
+    const uint32_t vbase = smem_u32(smem + C::OFF_VR + sv * C::TILE_BYTES);
     const uint32_t wbase = smem_u32(smem + C::OFF_WB + bj * C::WB_BYTES);
     const uint32_t dcol = tmem + 2 * C::NP + bj * C::NP;
 #pragma unroll
@@ -298,35 +325,28 @@ __device__ __forceinline__ bool gqa_mma_pv(uint8_t* smem, uint32_t tmem, int64_t
         const uint64_t bd = smem_desc(wbase + 512u * kk, 128u, 2048u, kLayoutNone);
         mma_i8(dcol, ad, bd, idesc, kk > 0);
     }
-    mma_commit(&o_full[bj]);
-    mma_commit(&empty[sj]);
+    mma_commit(&bars[C::B_OFULL + bj]);
+    mma_commit(&bars[C::B_VEMPTY + sv]);
     return true;
 }
 
-template <int G, int NS>
+template <int G, int NK, int NV>
 __device__ __forceinline__ void gqa_mma(const GqaParams& p, uint8_t* smem, uint32_t tmem) {
-    using C = GqaCfg<G, NS>;
+    using C = GqaCfg<G, NK, NV>;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-    uint64_t* full = bars;
-    uint64_t* s_full = bars + 2 * NS;
-    uint64_t* s_free = bars + 2 * NS + 2;
-    uint64_t* q_full = bars + 2 * NS + 10;
     constexpr uint32_t idesc_qk = idesc_i8(true, true, false, false, C::NP, 128);
     int64_t i = 0;
-    int s = 0;
-    uint32_t ph = 0;
-    int64_t prev_i = -1;
-    int prev_s = 0;
     int kq = 0;
     for (int it = blockIdx.x; it < p.n_items; it += p.grid, ++kq) {
         const GItem I = gqa_item(p, it);
         for (int tt = 0; tt < I.ntiles; ++tt, ++i) {
-            if (!mbar_wait(&full[s], ph)) return;
-            if (tt == 0 && !mbar_wait(&q_full[kq & 1], static_cast<uint32_t>((kq >> 1) & 1))) return;
+            const int sk = static_cast<int>(i % NK);
+            if (!mbar_wait(&bars[C::B_KFULL + sk], static_cast<uint32_t>((i / NK) & 1))) return;
+            if (tt == 0 && !mbar_wait(&bars[C::B_QFULL + (kq & 1)], static_cast<uint32_t>((kq >> 1) & 1))) return;
             const int bi = static_cast<int>(i & 1);
-            if (i >= 2 && !mbar_wait(&s_free[bi], static_cast<uint32_t>(((i >> 1) - 1) & 1))) return;
+            if (i >= 2 && !mbar_wait(&bars[C::B_SFREE + bi], static_cast<uint32_t>(((i >> 1) - 1) & 1))) return;
             tc_fence_after();
-            const uint32_t kbase = smem_u32(smem + s * C::STAGE_BYTES + C::OFF_K);
+            const uint32_t kbase = smem_u32(smem + C::OFF_KR + sk * C::TILE_BYTES);
             const uint32_t qbase = smem_u32(smem + C::OFF_QB + (kq & 1) * C::QB_BYTES);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
@@ -334,14 +354,12 @@ __device__ __forceinline__ void gqa_mma(const GqaParams& p, uint8_t* smem, uint3
                 const uint64_t bd = smem_desc(qbase + 32u * kk, 16u, 1024u, kLayoutSw128);
                 mma_i8(tmem + bi * C::NP, ad, bd, idesc_qk, kk > 0);
             }
-            mma_commit(&s_full[bi]);
-            if (prev_i >= 0 && !gqa_mma_pv<G, NS>(smem, tmem, prev_i, prev_s)) return;
-            prev_i = i;
-            prev_s = s;
-            if (++s == NS) { s = 0; ph ^= 1u; }
+            mma_commit(&bars[C::B_SFULL + bi]);
+            mma_commit(&bars[C::B_KEMPTY + sk]);
+            if (i >= 1 && !gqa_mma_pv<G, NK, NV>(smem, tmem, i - 1)) return;
         }
     }
-    if (prev_i >= 0) gqa_mma_pv<G, NS>(smem, tmem, prev_i, prev_s);
+    if (i >= 1) gqa_mma_pv<G, NK, NV>(smem, tmem, i - 1);
 }
 
 }  // namespace kvd
@@ -364,28 +382,44 @@ __device__ __forceinline__ void tmem_ld_np(uint32_t taddr, uint32_t (&r)[NP]) {
     }
 }
 
-// CTA-wide (4 epilogue warps) max or sum of K values per thread, bounded.
+// Warp-wide float max in one instruction (a NaN operand is ignored).
+__device__ __forceinline__ float warp_max(float x) {
+    float y;
+    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Max or sum of K values per thread over the 128 threads of one epilogue
+// warpgroup (4 warps), through shared memory and a bounded mbarrier wait.
+// Split in two so that independent work can run between posting the warp's
+// values and collecting the warpgroup result.
 template <int K, bool MAX>
-__device__ __forceinline__ bool epi_reduce(float (&v)[K], float* red, uint64_t* bar, uint32_t& use) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__device__ __forceinline__ void epi_reduce_post(float (&v)[K], float* red, uint64_t* bar, uint32_t use) {
+    const int wq = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-        float x = v[k];
+        if constexpr (MAX) {
+            v[k] = warp_max(v[k]);
+        } else {
+            float x = v[k];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float y = __shfl_xor_sync(0xffffffffu, x, o);
-            x = MAX ? fmaxf(x, y) : x + y;
+            for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+            v[k] = x;
         }
-        v[k] = x;
     }
     float* rb = red + (use & 1u) * 128;
     if (lane == 0) {
 #pragma unroll
-        for (int k = 0; k < K; ++k) rb[warp * 32 + k] = v[k];
+        for (int k = 0; k < K; ++k) rb[wq * 32 + k] = v[k];
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(bar);
+}
+
+template <int K, bool MAX>
+__device__ __forceinline__ bool epi_reduce_finish(float (&v)[K], float* red, uint64_t* bar, uint32_t& use) {
     const bool ok = mbar_wait(bar, use & 1u);
+    const float* rb = red + (use & 1u) * 128;
     ++use;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
@@ -395,44 +429,47 @@ __device__ __forceinline__ bool epi_reduce(float (&v)[K], float* red, uint64_t* 
     return ok;
 }
 
-// Query limbs of item `it` into buffer `buf`: thread r owns dim r of all G
-// heads. Qi = round(q * qscale * 2^E_h), |Qi| < 2^31, split into four signed
-// bytes written into the K-major 128-byte-swizzled B operand (row 4h + j).
-// Every thread ends with the same reduced maxima, so each one also keeps the
-// per-head scales 2^-E_h (sEn) in registers for the item's scores.
-template <int G, int NS>
+template <int K, bool MAX>
+__device__ __forceinline__ bool epi_reduce(float (&v)[K], float* red, uint64_t* bar, uint32_t& use) {
+    epi_reduce_post<K, MAX>(v, red, bar, use);
+    return epi_reduce_finish<K, MAX>(v, red, bar, use);
+}
+
+// Query limbs of item `it` into buffer `buf` for this warpgroup's heads:
+// thread r owns dim r. Qi = round(q * qscale * 2^E_h), |Qi| < 2^31, split into
+// four signed bytes written into the K-major 128-byte-swizzled B operand
+// (row 4h + j). Every thread of the warpgroup ends with the same reduced
+// maxima, so each keeps the per-head scales 2^-E_h (sEn) in registers.
+template <int G, int NK, int NV>
 __device__ __forceinline__ bool gqa_qlimbs(const GqaParams& p, uint8_t* smem, int it, int buf, uint32_t& use,
-                                           float (&sEn)[G]) {
-    using C = GqaCfg<G, NS>;
+                                           float (&sEn)[GqaCfg<G, NK, NV>::HPW]) {
+    using C = GqaCfg<G, NK, NV>;
+    constexpr int HPW = C::HPW;
+    const int wg = threadIdx.x >> 7, r = threadIdx.x & 127, lane = threadIdx.x & 31;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-    uint64_t* q_full = bars + 2 * NS + 10;
-    uint64_t* red_bar = bars + 2 * NS + 12;
-    float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
-    const int r = threadIdx.x, lane = threadIdx.x & 31;
+    uint64_t* q_full = bars + C::B_QFULL;
+    uint64_t* red_bar = bars + C::B_RED + wg;
+    float* red = reinterpret_cast<float*>(smem + C::OFF_RED) + wg * 256;
     const GItem I = gqa_item(p, it);
-    const float* q = p.Q + I.b * p.q_sb + static_cast<int64_t>(I.hk) * G * p.q_sh + r;
-    float qv[G], am[G];
+    const int h0 = wg * HPW;
+    const float* q = p.Q + I.b * p.q_sb + static_cast<int64_t>(I.hk * G + h0) * p.q_sh + r;
+    float qv[HPW], am[HPW];
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
+    for (int h = 0; h < HPW; ++h) {
         qv[h] = __ldg(q + h * p.q_sh) * p.qscale;
         am[h] = fabsf(qv[h]);
     }
-    if (!epi_reduce<G, true>(am, red, red_bar, use)) return false;
+    if (!epi_reduce<HPW, true>(am, red, red_bar, use)) return false;
     uint8_t* qb = smem + C::OFF_QB + buf * C::QB_BYTES;
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-        int E = 0;
-        if (am[h] > 0.f) {
-            int ex;
-            frexpf(am[h], &ex);  // am < 2^ex
-            E = min(126, max(-126, 30 - ex));
-        }
+    for (int h = 0; h < HPW; ++h) {
+        const int E = am[h] > 0.f ? min(126, max(-126, 30 - exp_above(am[h]))) : 0;  // |q| * 2^E < 2^30
         int qi = __float2int_rn(qv[h] * pow2i(E));
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int L = static_cast<int>(static_cast<int8_t>(qi & 0xFF));
             qi = (qi - L) >> 8;
-            const int n = 4 * h + j;
+            const int n = 4 * (h0 + h) + j;
             qb[(n >> 3) * 1024 + (n & 7) * 128 + ((((r >> 4) ^ (n & 7)) << 4) | (r & 15))] =
                 static_cast<uint8_t>(L);
         }
@@ -449,33 +486,36 @@ struct PvSnap {
     int it, flags;
 };
 
-template <int G, int NS>
+// PV epilogue of tile A.i for this warpgroup's heads (thread r = output dim r).
+template <int G, int NK, int NV>
 __device__ __forceinline__ bool gqa_pv_epi(const GqaParams& p, uint8_t* smem, uint32_t tmem, const PvSnap& A,
-                                           const float (&mA)[G], const int (&FA)[G], const float (&LA)[G],
-                                           float (&o)[G], float (&mpv)[G]) {
-    using C = GqaCfg<G, NS>;
-    constexpr int NP = C::NP;
+                                           const float (&mA)[GqaCfg<G, NK, NV>::HPW],
+                                           const int (&FA)[GqaCfg<G, NK, NV>::HPW],
+                                           const float (&LA)[GqaCfg<G, NK, NV>::HPW],
+                                           float (&o)[GqaCfg<G, NK, NV>::HPW], float (&mpv)[GqaCfg<G, NK, NV>::HPW]) {
+    using C = GqaCfg<G, NK, NV>;
+    constexpr int NP = C::NP, HPW = C::HPW, CPW = C::CPW;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-    uint64_t* o_full = bars + 2 * NS + 6;
-    uint64_t* o_free = bars + 2 * NS + 8;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = threadIdx.x;
+    uint64_t* o_full = bars + C::B_OFULL;
+    uint64_t* o_free = bars + C::B_OFREE;
+    const int wq = (threadIdx.x >> 5) & 3, wg = threadIdx.x >> 7, lane = threadIdx.x & 31, r = threadIdx.x & 127;
     const int bj = static_cast<int>(A.i & 1);
     if (!mbar_wait(&o_full[bj], static_cast<uint32_t>((A.i >> 1) & 1))) return false;
     tc_fence_after();
-    uint32_t orr[NP];
-    tmem_ld_np<NP>(tmem + (static_cast<uint32_t>(warp * 32) << 16) + 2 * NP + bj * NP, orr);
+    uint32_t orr[CPW];
+    tmem_ld_np<CPW>(tmem + (static_cast<uint32_t>(wq * 32) << 16) + 2 * NP + bj * NP + wg * CPW, orr);
     tmem_wait_ld();
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&o_free[bj]);
     if (A.flags & 1) {
 #pragma unroll
-        for (int h = 0; h < G; ++h) { o[h] = 0.f; mpv[h] = mA[h]; }
+        for (int h = 0; h < HPW; ++h) { o[h] = 0.f; mpv[h] = mA[h]; }
     }
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
+    for (int h = 0; h < HPW; ++h) {
         const float f = combine_limbs(orr[4 * h], orr[4 * h + 1], orr[4 * h + 2], orr[4 * h + 3]);
-        const float al = (mpv[h] == mA[h]) ? 1.f : exp2f(mpv[h] - mA[h]);
+        const float al = (mpv[h] == mA[h]) ? 1.f : ex2_fast(mpv[h] - mA[h]);
         o[h] = fmaf(f, pow2i(-FA[h]), o[h] * al);
         mpv[h] = mA[h];
     }
@@ -483,8 +523,8 @@ __device__ __forceinline__ bool gqa_pv_epi(const GqaParams& p, uint8_t* smem, ui
         const GItem I = gqa_item(p, A.it);
         const bool records = p.P > 1 || (p.flags & KVD_FLAG_PARTIAL_OUT);
 #pragma unroll
-        for (int h = 0; h < G; ++h) {
-            const int hq = I.hk * G + h;
+        for (int h = 0; h < HPW; ++h) {
+            const int hq = I.hk * G + wg * HPW + h;
             float* row = p.out + I.b * p.o_sb + static_cast<int64_t>(hq) * p.o_sh;
             if (!records) {
                 row[r] = LA[h] > 0.f ? o[h] / LA[h] : 0.f;
@@ -500,34 +540,44 @@ __device__ __forceinline__ bool gqa_pv_epi(const GqaParams& p, uint8_t* smem, ui
     return true;
 }
 
-template <int G, int NS>
+// One epilogue warpgroup: scores, online softmax and weight limbs of every
+// tile for heads [wg*HPW, (wg+1)*HPW), then the PV epilogue one tile behind.
+template <int G, int NK, int NV>
 __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, uint32_t tmem) {
-    using C = GqaCfg<G, NS>;
-    constexpr int NP = C::NP;
+    using C = GqaCfg<G, NK, NV>;
+    constexpr int NP = C::NP, HPW = C::HPW, CPW = C::CPW;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-    uint64_t* full = bars;
-    uint64_t* empty = bars + NS;
-    uint64_t* s_full = bars + 2 * NS;
-    uint64_t* s_free = bars + 2 * NS + 2;
-    uint64_t* w_full = bars + 2 * NS + 4;
-    uint64_t* red_bar = bars + 2 * NS + 12;
+    uint64_t* vfull = bars + C::B_VFULL;
+    uint64_t* vempty = bars + C::B_VEMPTY;
+    uint64_t* s_full = bars + C::B_SFULL;
+    uint64_t* s_free = bars + C::B_SFREE;
+    uint64_t* w_full = bars + C::B_WFULL;
+    const int wq = (threadIdx.x >> 5) & 3, wg = threadIdx.x >> 7, lane = threadIdx.x & 31, r = threadIdx.x & 127;
+    uint64_t* red_bar = bars + C::B_RED + wg;
+    float* red = reinterpret_cast<float*>(smem + C::OFF_RED) + wg * 256;
     const GMeta* meta = reinterpret_cast<const GMeta*>(smem + C::OFF_META);
-    float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = threadIdx.x;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16) + wg * CPW;
     uint32_t use = 0;
 
-    // Zero both query-limb buffers (pad rows must stay zero), then item 0's limbs.
-    for (int x = r; x < 2 * C::QB_BYTES / 16; x += 128)
-        reinterpret_cast<uint4*>(smem + C::OFF_QB)[x] = make_uint4(0u, 0u, 0u, 0u);
-    float sEn[G];
-    if (!gqa_qlimbs<G, NS>(p, smem, blockIdx.x, 0, use, sEn)) return;
+    // Zero this warpgroup's rows of both query-limb buffers (pad rows stay
+    // zero), then item 0's limbs (its reduction orders the zeroing first).
+    {
+        const int rows = NP / C::NWG;
+        for (int x = r; x < 2 * rows * 8; x += 128) {
+            const int buf = x / (rows * 8), rem = x % (rows * 8);
+            const int n = wg * rows + rem / 8, chunk = rem % 8;
+            *reinterpret_cast<uint4*>(smem + C::OFF_QB + buf * C::QB_BYTES + (n >> 3) * 1024 + (n & 7) * 128 +
+                                      chunk * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+    float sEn[HPW];
+    if (!gqa_qlimbs<G, NK, NV>(p, smem, blockIdx.x, 0, use, sEn)) return;
 
-    float m[G], l[G], sE[G], o[G], mpv[G], mA[G], LA[G];
-    int FA[G];
+    float m[HPW], l[HPW], sE[HPW], o[HPW], mpv[HPW], mA[HPW], LA[HPW];
+    int FA[HPW];
 #pragma unroll
-    for (int h = 0; h < G; ++h) { m[h] = -INFINITY; l[h] = 0.f; sE[h] = 1.f; o[h] = 0.f; mpv[h] = -INFINITY;
-                                  mA[h] = -INFINITY; LA[h] = 0.f; FA[h] = 0; }
+    for (int h = 0; h < HPW; ++h) { m[h] = -INFINITY; l[h] = 0.f; sE[h] = 1.f; o[h] = 0.f; mpv[h] = -INFINITY;
+                                    mA[h] = -INFINITY; LA[h] = 0.f; FA[h] = 0; }
     PvSnap A{-1, 0, 0};
     int64_t i = 0;
     int s = 0;
@@ -540,131 +590,141 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
             // ---- scores of tile i (thread r = token r of the tile)
             if (!mbar_wait(&s_full[bi], static_cast<uint32_t>((i >> 1) & 1))) return;
             tc_fence_after();
-            uint32_t sr[NP];
-            tmem_ld_np<NP>(lane_base + bi * NP, sr);
+            uint32_t sr[CPW];
+            tmem_ld_np<CPW>(lane_base + bi * NP, sr);
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_free[bi]);
-            if (!mbar_wait(&full[s], ph)) return;
+            if (!mbar_wait(&vfull[s], ph)) return;  // metadata and scale windows of tile i
             const GMeta mt = meta[s];
             if (tt == 0) {
 #pragma unroll
-                for (int h = 0; h < G; ++h) { m[h] = -INFINITY; l[h] = 0.f; sE[h] = sEn[h]; }
+                for (int h = 0; h < HPW; ++h) { m[h] = -INFINITY; l[h] = 0.f; sE[h] = sEn[h]; }
             }
             const bool valid = r < mt.n;
-            const float* ksm = reinterpret_cast<const float*>(smem + s * C::STAGE_BYTES + C::OFF_KS);
-            const float* vsm = reinterpret_cast<const float*>(smem + s * C::STAGE_BYTES + C::OFF_VS);
+            const float* ksm = reinterpret_cast<const float*>(smem + C::OFF_SC + s * C::SC_BYTES);
+            const float* vsm = ksm + C::SC_FLOATS;
             const float ksv = valid ? ksm[(mt.offs & 0xff) + r] : 0.f;
             const float vsv = valid ? vsm[(mt.offs >> 8) + r] : 0.f;
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-            if (++s == NS) { s = 0; ph ^= 1u; }
-            float sc[G], rv[G + 1];
+            if (lane == 0) mbar_arrive(&vempty[s]);
+            if (++s == NV) { s = 0; ph ^= 1u; }
+            float sc[HPW], rv[HPW + 1];
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
+            for (int h = 0; h < HPW; ++h) {
                 const float dot = combine_limbs(sr[4 * h], sr[4 * h + 1], sr[4 * h + 2], sr[4 * h + 3]);
                 sc[h] = valid ? dot * sE[h] * ksv : -INFINITY;
                 rv[h] = sc[h];
             }
-            rv[G] = vsv;
-            if (!epi_reduce<G + 1, true>(rv, red, red_bar, use)) return;
-            const float vsmax = rv[G];
+            rv[HPW] = vsv;
+            // Post this tile's maxima, run the previous tile's PV epilogue
+            // (thread r = output dim r) while the other warps catch up, then
+            // collect the warpgroup maxima.
+            epi_reduce_post<HPW + 1, true>(rv, red, red_bar, use);
+            if (A.i >= 0 && !gqa_pv_epi<G, NK, NV>(p, smem, tmem, A, mA, FA, LA, o, mpv)) return;
+            if (!epi_reduce_finish<HPW + 1, true>(rv, red, red_bar, use)) return;
+            const float vsmax = rv[HPW];
             // ---- online softmax (base 2, lazy max) and the weight limbs
-            uint32_t W[NP / 4];
+            uint32_t W[CPW / 4];
 #pragma unroll
-            for (int x = 0; x < NP / 4; ++x) W[x] = 0u;
-            int FB[G];
+            for (int x = 0; x < CPW / 4; ++x) W[x] = 0u;
+            int FB[HPW];
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
-                const float tmax = rv[h];
-                const float mnew = (tmax > m[h] + 8.f) ? tmax : m[h];
-                const float alpha = (mnew == -INFINITY) ? 1.f : exp2f(m[h] - mnew);
-                l[h] *= alpha;
-                m[h] = mnew;
-                const float pr = valid ? exp2f(sc[h] - m[h]) : 0.f;
+            for (int h = 0; h < HPW; ++h) {
+                const float tmax = rv[h];  // same in every thread of the warpgroup
+                if (tmax > m[h] + 8.f) {
+                    l[h] *= ex2_fast(m[h] - tmax);  // 0 while m is still -inf
+                    m[h] = tmax;
+                }
+                const float pr = valid ? ex2_fast(sc[h] - m[h]) : 0.f;
                 l[h] += pr;
-                const float bound = (tmax == -INFINITY) ? 0.f : exp2f(tmax - m[h]) * vsmax;
+                // Weight exponent: p <= 2^(tmax - m) <= 2^ceil(tmax - m) and v_scale < 2^exp_above(vsmax),
+                // so w * 2^F < 2^30 with F = 30 - ceil(tmax - m) - exp_above(vsmax).
                 int F = 0;
-                if (bound > 0.f) {
-                    int ex;
-                    frexpf(bound, &ex);  // bound < 2^ex, so w * 2^(31-ex) < 2^31
-                    F = min(126, max(-126, 31 - ex));
+                if (tmax != -INFINITY) {
+                    const float d = tmax - m[h];
+                    const int ep = d > -126.f ? static_cast<int>(ceilf(d)) : -126;
+                    F = min(126, max(-126, 30 - ep - exp_above(vsmax)));
                 }
                 FB[h] = F;
                 W[h] = valid ? __float2uint_rn(pr * vsv * pow2i(F)) : 0u;
             }
             uint8_t* wb = smem + C::OFF_WB + bi * C::WB_BYTES;
 #pragma unroll
-            for (int g = 0; g < NP / 16; ++g)
-                *reinterpret_cast<uint4*>(wb + g * 2048 + r * 16) = make_uint4(W[4 * g], W[4 * g + 1], W[4 * g + 2], W[4 * g + 3]);
+            for (int g = 0; g < CPW / 16; ++g)
+                *reinterpret_cast<uint4*>(wb + (wg * (CPW / 16) + g) * 2048 + r * 16) =
+                    make_uint4(W[4 * g], W[4 * g + 1], W[4 * g + 2], W[4 * g + 3]);
             fence_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&w_full[bi]);
-            float LB[G];
+            float LB[HPW];
             if (tt == I.ntiles - 1) {
 #pragma unroll
-                for (int h = 0; h < G; ++h) LB[h] = l[h];
-                if (!epi_reduce<G, false>(LB, red, red_bar, use)) return;
+                for (int h = 0; h < HPW; ++h) LB[h] = l[h];
+                if (!epi_reduce<HPW, false>(LB, red, red_bar, use)) return;
             } else {
 #pragma unroll
-                for (int h = 0; h < G; ++h) LB[h] = 0.f;
+                for (int h = 0; h < HPW; ++h) LB[h] = 0.f;
             }
             if (tt == 0 && it + p.grid < p.n_items) {
-                if (!gqa_qlimbs<G, NS>(p, smem, it + p.grid, (kq + 1) & 1, use, sEn)) return;
+                if (!gqa_qlimbs<G, NK, NV>(p, smem, it + p.grid, (kq + 1) & 1, use, sEn)) return;
             }
-            // ---- PV epilogue of the previous tile (thread r = output dim r)
-            if (A.i >= 0 && !gqa_pv_epi<G, NS>(p, smem, tmem, A, mA, FA, LA, o, mpv)) return;
 #pragma unroll
-            for (int h = 0; h < G; ++h) { mA[h] = m[h]; FA[h] = FB[h]; LA[h] = LB[h]; }
+            for (int h = 0; h < HPW; ++h) { mA[h] = m[h]; FA[h] = FB[h]; LA[h] = LB[h]; }
             A.i = i;
             A.it = it;
             A.flags = mt.flags;
         }
     }
-    if (A.i >= 0) gqa_pv_epi<G, NS>(p, smem, tmem, A, mA, FA, LA, o, mpv);
+    if (A.i >= 0) gqa_pv_epi<G, NK, NV>(p, smem, tmem, A, mA, FA, LA, o, mpv);
 }
 
-template <int G, int NS, int MINB>
-__global__ void __launch_bounds__(192, MINB) gqa_tc_kernel(const __grid_constant__ CUtensorMap kmap,
-                                                          const __grid_constant__ CUtensorMap vmap,
-                                                          const GqaParams p) {
-    using C = GqaCfg<G, NS>;
+template <int G, int NK, int NV, int MINB>
+__global__ void __launch_bounds__(GqaCfg<G, NK, NV>::THREADS, MINB) gqa_tc_kernel(
+    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const GqaParams p) {
+    using C = GqaCfg<G, NK, NV>;
+    constexpr int EW = 4 * C::NWG;  // epilogue warps; then the producer warp, then the MMA warp
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     if (static_cast<int>(blockIdx.x) >= p.n_items) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-    uint64_t* done = bars + 2 * NS + 13;
-    uint64_t* drain = bars + 2 * NS + 14;
+    uint64_t* done = bars + C::B_DONE;
+    uint64_t* drain = bars + C::B_DRAIN;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < NS; ++s) {
-            mbar_init(&bars[s], 1);          // full
-            mbar_init(&bars[NS + s], 5);     // empty: MMA commit + 4 epilogue warps
+        for (int s = 0; s < NK; ++s) {
+            mbar_init(&bars[C::B_KFULL + s], 1);       // producer arrive + transaction bytes
+            mbar_init(&bars[C::B_KEMPTY + s], 1);      // QK commit
         }
-        const int b0 = 2 * NS;
-        mbar_init(&bars[b0 + 0], 1);  mbar_init(&bars[b0 + 1], 1);   // s_full
-        mbar_init(&bars[b0 + 2], 4);  mbar_init(&bars[b0 + 3], 4);   // s_free
-        mbar_init(&bars[b0 + 4], 4);  mbar_init(&bars[b0 + 5], 4);   // w_full
-        mbar_init(&bars[b0 + 6], 1);  mbar_init(&bars[b0 + 7], 1);   // o_full
-        mbar_init(&bars[b0 + 8], 4);  mbar_init(&bars[b0 + 9], 4);   // o_free
-        mbar_init(&bars[b0 + 10], 4); mbar_init(&bars[b0 + 11], 4);  // q_full
-        mbar_init(&bars[b0 + 12], 4);                                // red
-        mbar_init(done, 4);
+        for (int s = 0; s < NV; ++s) {
+            mbar_init(&bars[C::B_VFULL + s], 1);       // producer arrive + transaction bytes
+            mbar_init(&bars[C::B_VEMPTY + s], 1 + EW); // PV commit + every epilogue warp
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars[C::B_SFULL + b], 1);
+            mbar_init(&bars[C::B_SFREE + b], EW);
+            mbar_init(&bars[C::B_WFULL + b], EW);
+            mbar_init(&bars[C::B_OFULL + b], 1);
+            mbar_init(&bars[C::B_OFREE + b], EW);
+            mbar_init(&bars[C::B_QFULL + b], EW);
+        }
+        for (int wg = 0; wg < C::NWG; ++wg) mbar_init(&bars[C::B_RED + wg], 4);
+        mbar_init(done, EW);
         mbar_init(drain, 1);
         fence_mbar_init();
     }
-    if (warp == 5) tmem_alloc(reinterpret_cast<uint32_t*>(smem + C::OFF_TMEM), C::TMEM_COLS);
+    if (warp == EW + 1) tmem_alloc(reinterpret_cast<uint32_t*>(smem + C::OFF_TMEM), C::TMEM_COLS);
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + C::OFF_TMEM);
-    if (warp == 4) {
-        if (lane == 0) gqa_producer<G, NS>(&kmap, &vmap, p, smem);
+    if (warp == EW) {
+        if (lane < 2) gqa_producer<G, NK, NV>(&kmap, &vmap, p, smem, lane == 1);
         return;
     }
-    if (warp == 5) {
+    if (warp == EW + 1) {
         if (lane == 0) {
-            gqa_mma<G, NS>(p, smem, tmem);
+            gqa_mma<G, NK, NV>(p, smem, tmem);
             mma_commit(drain);  // arrives once every MMA issued above has completed
             mbar_wait(drain, 0);
             mbar_wait(done, 0);  // epilogue warps have finished reading TMEM
@@ -674,7 +734,7 @@ __global__ void __launch_bounds__(192, MINB) gqa_tc_kernel(const __grid_constant
         tmem_dealloc(tmem, C::TMEM_COLS);
         return;
     }
-    gqa_epilogue<G, NS>(p, smem, tmem);
+    gqa_epilogue<G, NK, NV>(p, smem, tmem);
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(done);
@@ -686,7 +746,8 @@ __global__ void __launch_bounds__(192, MINB) gqa_tc_kernel(const __grid_constant
 namespace kvd {
 namespace {
 
-constexpr int kGqaNS = KVD_GQA_NS;
+constexpr int kGqaNK = KVD_GQA_NK;
+constexpr int kGqaNV = KVD_GQA_NV;
 constexpr int kGqaCtas = KVD_GQA_CTAS;
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -732,12 +793,12 @@ int gqa_split_count(const kvd_decode_desc& d) {
 
 template <int G>
 cudaError_t launch_gqa_g(const CUtensorMap& km, const CUtensorMap& vm, const GqaParams& p, cudaStream_t st) {
-    using C = GqaCfg<G, kGqaNS>;
+    using C = GqaCfg<G, kGqaNK, kGqaNV>;
     static bool configured[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    auto kern = gqa_tc_kernel<G, kGqaNS, kGqaCtas>;
+    auto kern = gqa_tc_kernel<G, kGqaNK, kGqaNV, kGqaCtas>;
     if (dev < 64 && !configured[dev]) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
         if (e != cudaSuccess) return e;
