@@ -1,0 +1,62 @@
+"""Worker for tests/test_mgpu_gpu.py, launched with torch.distributed.run (one
+rank per GPU, NCCL). Checks, against the FP64 oracle:
+  * sequence split: each rank decodes its token shard into partial records,
+    records are all-gathered over NCCL and merged by the combine kernel;
+  * batch shards: each rank decodes its own sequences with no communication.
+Exits 0 only if every rank's results are within the decode tolerance."""
+import datetime
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path[:0] = [os.path.join(ROOT, "cuda-operators_b200"), os.path.join(ROOT, "oracle")]
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+import kvd_mgpu as mg  # noqa: E402
+import kvdecode as kvd  # noqa: E402
+import pyoracle as po  # noqa: E402
+
+
+def main() -> int:
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    bad = 0
+    try:
+        for (B, Hq, Hkv, S) in [(2, 8, 8, 4096), (2, 16, 2, 3000)]:
+            q, K, V, ks, vs = po.random_cache(11 + Hq, B, Hq, Hkv, S, 128)  # same on every rank
+            ref = po.decode_f64(q, K, V, ks, vs)
+            lo, hi = mg.seq_shard(S, world, rank, align=128)
+            shard = [torch.from_numpy(np.ascontiguousarray(a[:, :, lo:hi])).to(dev) for a in (K, V, ks, vs)]
+            dec = mg.SeqSplitDecode(B, Hq, 128, dev)
+            for _ in range(2):
+                out = dec(torch.from_numpy(q).to(dev), *shard)
+                torch.cuda.synchronize()
+                b, err, _ = po.check(out.cpu().numpy(), ref)
+                bad += b
+                print(f"[rank {rank}] seq split B={B} Hq={Hq} Hkv={Hkv} S={S} shard=[{lo},{hi}) "
+                      f"max_abs={err:.3g} bad={b}", flush=True)
+            # batch shards: no communication
+            b0, b1 = mg.batch_shard(B, world, rank)
+            if b1 > b0:
+                tq, tK, tV, tks, tvs = (torch.from_numpy(np.ascontiguousarray(a[b0:b1])).to(dev)
+                                        for a in (q, K, V, ks, vs))
+                out = kvd.decode(tq, tK, tV, tks, tvs)
+                torch.cuda.synchronize()
+                b, err, _ = po.check(out.cpu().numpy(), ref[b0:b1])
+                bad += b
+        flag = torch.tensor([bad], device=dev)
+        dist.all_reduce(flag)
+        bad = int(flag.item())
+    finally:
+        dist.destroy_process_group()
+    return 0 if bad == 0 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
