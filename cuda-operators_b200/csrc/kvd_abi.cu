@@ -74,7 +74,7 @@ extern "C" size_t kvd_workspace_size(const kvd_decode_desc* desc) {
                static_cast<size_t>(2) * device_sm_count() * sk_ctas_per_sm(d.head_dim) * (d.head_dim + 4) *
                    sizeof(float);
     const size_t gen = generic_workspace_size(d);
-    const size_t gqa = d.num_q_heads > d.num_kv_heads && gqa_path_ok(d) ? gqa_workspace_size(d) : 0;
+    const size_t gqa = gqa_path_ok(d) ? gqa_workspace_size(d) : 0;
     size_t need = fast > gen ? fast : gen;
     return need > gqa ? need : gqa;
 }
@@ -96,8 +96,11 @@ extern "C" cudaError_t kvd_decode_launch(const kvd_decode_desc* desc, const floa
         return launch_generic(d, Q, K, V, k_scale, v_scale, out, workspace, workspace_bytes, stream,
                               &tl_launches);
 
-    // Grouped-query heads share every K/V tile: tensor-core kernel.
-    if (d.num_q_heads > d.num_kv_heads && gqa_path_ok(d))
+    // Grouped-query heads share every K/V tile: tensor-core kernel. MHA with
+    // D=128 takes it too: the tensor cores do QK and PV, so the SMs spend far
+    // fewer instructions (and watts) per byte than the CUDA-core kernel.
+    const bool mha_tc = KVD_MHA_TENSOR_CORES >= 2 || (KVD_MHA_TENSOR_CORES == 1 && !d.seq_lens);
+    if ((d.num_q_heads > d.num_kv_heads || mha_tc) && gqa_path_ok(d))
         return launch_gqa_tc(d, Q, K, V, k_scale, v_scale, out, workspace, workspace_bytes, stream, &tl_launches);
 
     const int tok = tile_tokens(d.head_dim);

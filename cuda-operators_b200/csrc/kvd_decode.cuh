@@ -53,6 +53,12 @@ struct DecodeParams {
 #define KVD_SK64_CTAS 2
 #endif
 
+// Route MHA with head_dim 128 to the tensor-core kernel: 1 = dense batches,
+// 2 = dense and ragged batches, 0 = never (CUDA-core split-KV kernel).
+#ifndef KVD_MHA_TENSOR_CORES
+#define KVD_MHA_TENSOR_CORES 2
+#endif
+
 // K ring stages, V ring stages and resident CTAs per SM of the tcgen05 GQA kernel.
 #ifndef KVD_GQA_NK
 #define KVD_GQA_NK 3

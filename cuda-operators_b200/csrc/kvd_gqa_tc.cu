@@ -781,14 +781,28 @@ bool make_kv_map(CUtensorMap* m, const int8_t* base, int B, int Hkv, int cap, in
     return r == CUDA_SUCCESS;
 }
 
+// Splits per (batch, kv head) item. Items are dealt round-robin to the
+// persistent CTAs, so pick the split count P that minimises
+// rounds(P) * (tiles per item + 1), the +1 standing for the per-item cost
+// (query limbs, output write); P > 1 also costs a record-combine launch.
 int gqa_split_count(const kvd_decode_desc& d) {
     const int64_t units = static_cast<int64_t>(d.batch) * d.num_kv_heads;
-    const int64_t grid_max = static_cast<int64_t>(device_sm_count()) * kGqaCtas;
-    if (units >= grid_max) return 1;
-    const int max_by_len = d.max_seq_len > 0 ? (d.max_seq_len + 127) / 128 : 1;
-    int64_t P = (grid_max + units - 1) / units;
-    if (P > max_by_len) P = max_by_len;
-    return static_cast<int>(P < 1 ? 1 : P);
+    const int64_t grid = static_cast<int64_t>(device_sm_count()) * kGqaCtas;
+    const int S = d.max_seq_len > 0 ? d.max_seq_len : 1;
+    const int max_tiles = (S + 127) / 128;
+    int best_p = 1;
+    double best = -1.0;
+    for (int P = 1; P <= max_tiles && P <= 256; ++P) {
+        const int span = ((((S + P - 1) / P) + 127) / 128) * 128;
+        const int pe = (S + span - 1) / span;
+        if (pe != P) continue;
+        const int64_t items = units * P;
+        const double rounds = static_cast<double>((items + grid - 1) / grid);
+        const double cost = rounds * (span / 128 + 1) + (P > 1 ? 2.0 : 0.0);
+        if (best < 0 || cost < best) { best = cost; best_p = P; }
+        if (items >= 64 * grid) break;
+    }
+    return best_p;
 }
 
 template <int G>
@@ -813,7 +827,7 @@ cudaError_t launch_gqa_g(const CUtensorMap& km, const CUtensorMap& vm, const Gqa
 bool gqa_path_ok(const kvd_decode_desc& d) {
     const int G = d.num_q_heads / d.num_kv_heads;
     if (d.head_dim != 128 || d.max_seq_len < 1) return false;
-    if (G != 2 && G != 4 && G != 8 && G != 16) return false;
+    if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16) return false;
     return tensor_map_encoder() != nullptr;
 }
 
@@ -858,6 +872,7 @@ cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const float* Q, const int8_t
     p.flags = d.flags;
     cudaError_t e;
     switch (G) {
+        case 1: e = launch_gqa_g<1>(km, vm, p, st); break;
         case 2: e = launch_gqa_g<2>(km, vm, p, st); break;
         case 4: e = launch_gqa_g<4>(km, vm, p, st); break;
         case 8: e = launch_gqa_g<8>(km, vm, p, st); break;
