@@ -353,7 +353,9 @@ def run_ours(args) -> None:
         "roofline": {"bound": "hbm", "achieved": per_gpu_gbs, "peak": peak, "unit": "GB/s",
                      "frac": per_gpu_gbs / peak, "peak_source": f"{peak_kind} copy bandwidth",
                      "traffic": committed_traffic(args.config),
-                     "timed": "split-KV decode step (main kernel + boundary combine)"},
+                     "timed": ("decode step: tcgen05 kernel gqa_tc_kernel" if cfg.head_dim == 128
+                               else "decode step: CUDA-core split-KV kernel + boundary combine")
+                              + (" + NCCL record all-gather + LSE combine" if seqsplit else "")},
         "clocks": clk.summary(),
         "e2e": {"value": e2e_gbs, "unit": "GB/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": int(q_host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4),
