@@ -126,8 +126,14 @@ extern "C" cudaError_t kvd_decode_launch(const kvd_decode_desc* desc, const floa
     int64_t grid = static_cast<int64_t>(device_sm_count()) * sk_ctas_per_sm(d.head_dim);  // persistent CTAs
     if (!d.seq_lens) {
         p.tiles_per_head = d.max_seq_len > 0 ? (d.max_seq_len + tok - 1) / tok : 1;
-        p.n_tiles = static_cast<int64_t>(d.batch) * d.num_q_heads * p.tiles_per_head;
+        const int64_t heads = static_cast<int64_t>(d.batch) * d.num_q_heads;
+        p.n_tiles = heads * p.tiles_per_head;
         if (grid > p.n_tiles) grid = p.n_tiles;
+        // Small problems: one CTA per whole head needs no combine launch; take it
+        // when its tile count does not exceed the split's rounds plus the combine
+        // (about 8 tiles of work).
+        const int64_t split_rounds = (p.n_tiles + grid - 1) / grid;
+        if (heads <= grid && p.tiles_per_head <= split_rounds + 8) grid = heads;
     } else {
         p.tile_prefix = static_cast<const int32_t*>(workspace);
     }

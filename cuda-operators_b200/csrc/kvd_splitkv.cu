@@ -514,7 +514,10 @@ cudaError_t launch_sk(const DecodeParams& p, cudaStream_t st, int* launches) {
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     ++*launches;
-    if (p.grid > 1) {
+    // Dense batches whose CTA ranges all start at a head boundary split no head.
+    const bool whole_heads = p.tile_prefix == nullptr && p.n_tiles % p.grid == 0 &&
+                             (p.n_tiles / p.grid) % p.tiles_per_head == 0;
+    if (p.grid > 1 && !whole_heads) {
         splitkv_combine_kernel<C::TOK><<<p.grid - 1, 128, 0, st>>>(p);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
