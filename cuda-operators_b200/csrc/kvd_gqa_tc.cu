@@ -190,12 +190,12 @@ __device__ __forceinline__ float small_int_to_float(uint32_t v) {
     return __uint_as_float(0x4B400000u + v) - 12582912.0f;
 }
 
-// Four exact limb sums -> fp32 value of sum_j acc_j 2^(8j).
+// Four exact limb sums (|acc_j| < 2^22) -> fp32 value of sum_j acc_j 2^(8j).
+// Pairs are joined exactly in int32 (|hi|, |lo| < 2^30), then converted.
 __device__ __forceinline__ float combine_limbs(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3) {
-    float f = small_int_to_float(a3) * 16777216.0f;
-    f = fmaf(small_int_to_float(a2), 65536.0f, f);
-    f = fmaf(small_int_to_float(a1), 256.0f, f);
-    return f + small_int_to_float(a0);
+    const int hi = static_cast<int>(a3) * 256 + static_cast<int>(a2);
+    const int lo = static_cast<int>(a1) * 256 + static_cast<int>(a0);
+    return fmaf(__int2float_rn(hi), 65536.0f, __int2float_rn(lo));
 }
 
 __device__ __forceinline__ float pow2i(int e) {  // 2^e for e in [-126, 127]
