@@ -46,6 +46,7 @@ struct GqaParams {
     float* out;
     float* partials;           // [B*Hq][P] records of D+4 floats when P > 1
     const int32_t* seq_lens;   // device [B] or nullptr
+    const int32_t* order;      // ragged: sequences sorted by length, longest first; else nullptr
     int B, Hq, Hkv, S, P, span, n_items, grid;
     int64_t sc_sb, sc_sh, q_sb, q_sh, o_sb, o_sh;
     float qscale;
@@ -222,18 +223,40 @@ struct GItem {
     int b, hk, split, t_lo, t_hi, ntiles;
 };
 
+// Items are numbered split-major: item = (split * B + k) * Hkv + hk, where k
+// walks the sequences longest first for ragged batches. Dealt round-robin to
+// the CTAs, long items therefore go out first (longest-processing-time
+// order). A split past the end of its sequence is empty (no tiles) and is
+// skipped by every role, except split 0 of an empty sequence, which still
+// writes its zero output.
+__device__ __forceinline__ int seq_len_of(const GqaParams& p, int b) {
+    return p.seq_lens ? min(max(0, __ldg(p.seq_lens + b)), p.S) : p.S;
+}
+
+__device__ __forceinline__ int split_count(const GqaParams& p, int len) {
+    return len > 0 ? (len + p.span - 1) / p.span : 1;
+}
+
 __device__ __forceinline__ GItem gqa_item(const GqaParams& p, int it) {
     GItem I;
-    const int u = it / p.P;
-    I.split = it - u * p.P;
-    I.b = u / p.Hkv;
-    I.hk = u - I.b * p.Hkv;
-    const int len = p.seq_lens ? min(max(0, __ldg(p.seq_lens + I.b)), p.S) : p.S;
+    const int per_split = p.B * p.Hkv;
+    I.split = it / per_split;
+    const int rem = it - I.split * per_split;
+    const int k = rem / p.Hkv;
+    I.hk = rem - k * p.Hkv;
+    I.b = p.order ? __ldg(p.order + k) : k;
+    const int len = seq_len_of(p, I.b);
     I.t_lo = I.split * p.span;
     I.t_hi = min(len, I.t_lo + p.span);
     const int n = I.t_hi - I.t_lo;
-    I.ntiles = n > 0 ? (n + 127) / 128 : 1;
+    I.ntiles = n > 0 ? (n + 127) / 128 : (I.split == 0 ? 1 : 0);
     return I;
+}
+
+// First non-empty item of this CTA at or after `it` (stepping by the grid).
+__device__ __forceinline__ int next_item(const GqaParams& p, int it) {
+    while (it < p.n_items && gqa_item(p, it).ntiles == 0) it += p.grid;
+    return it;
 }
 
 struct __align__(16) GMeta {
@@ -258,7 +281,7 @@ __device__ __forceinline__ void gqa_producer(const CUtensorMap* kmap, const CUte
     uint32_t round_par = 0;
     bool wrapped = false, ok = true;
     int64_t issued = 0;
-    for (int it = blockIdx.x; it < p.n_items && ok; it += p.grid) {
+    for (int it = next_item(p, blockIdx.x); it < p.n_items && ok; it = next_item(p, it + p.grid)) {
         const GItem I = gqa_item(p, it);
         for (int tt = 0; tt < I.ntiles; ++tt) {
             if (wrapped && !mbar_wait(&empty[s], round_par ^ 1u)) { ok = false; break; }
@@ -337,7 +360,7 @@ __device__ __forceinline__ void gqa_mma(const GqaParams& p, uint8_t* smem, uint3
     constexpr uint32_t idesc_qk = idesc_i8(true, true, false, false, C::NP, 128);
     int64_t i = 0;
     int kq = 0;
-    for (int it = blockIdx.x; it < p.n_items; it += p.grid, ++kq) {
+    for (int it = next_item(p, blockIdx.x); it < p.n_items; it = next_item(p, it + p.grid), ++kq) {
         const GItem I = gqa_item(p, it);
         for (int tt = 0; tt < I.ntiles; ++tt, ++i) {
             const int sk = static_cast<int>(i % NK);
@@ -521,7 +544,8 @@ __device__ __forceinline__ bool gqa_pv_epi(const GqaParams& p, uint8_t* smem, ui
     }
     if (A.flags & 2) {
         const GItem I = gqa_item(p, A.it);
-        const bool records = p.P > 1 || (p.flags & KVD_FLAG_PARTIAL_OUT);
+        const bool split_row = p.P > 1 && split_count(p, seq_len_of(p, I.b)) > 1;
+        const bool records = split_row || (p.flags & KVD_FLAG_PARTIAL_OUT);
 #pragma unroll
         for (int h = 0; h < HPW; ++h) {
             const int hq = I.hk * G + wg * HPW + h;
@@ -529,7 +553,7 @@ __device__ __forceinline__ bool gqa_pv_epi(const GqaParams& p, uint8_t* smem, ui
             if (!records) {
                 row[r] = LA[h] > 0.f ? o[h] / LA[h] : 0.f;
             } else {
-                float* rec = p.P > 1
+                float* rec = split_row
                     ? p.partials + ((static_cast<int64_t>(I.b) * p.Hq + hq) * p.P + I.split) * (C::D + 4)
                     : row;
                 if (r == 0) { rec[0] = mA[h]; rec[1] = LA[h]; }
@@ -571,7 +595,7 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
         }
     }
     float sEn[HPW];
-    if (!gqa_qlimbs<G, NK, NV>(p, smem, blockIdx.x, 0, use, sEn)) return;
+    if (!gqa_qlimbs<G, NK, NV>(p, smem, next_item(p, blockIdx.x), 0, use, sEn)) return;
 
     float m[HPW], l[HPW], sE[HPW], o[HPW], mpv[HPW], mA[HPW], LA[HPW];
     int FA[HPW];
@@ -583,7 +607,7 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
     int s = 0;
     uint32_t ph = 0;
     int kq = 0;
-    for (int it = blockIdx.x; it < p.n_items; it += p.grid, ++kq) {
+    for (int it = next_item(p, blockIdx.x); it < p.n_items; it = next_item(p, it + p.grid), ++kq) {
         const GItem I = gqa_item(p, it);
         for (int tt = 0; tt < I.ntiles; ++tt, ++i) {
             const int bi = static_cast<int>(i & 1);
@@ -667,8 +691,9 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
 #pragma unroll
                 for (int h = 0; h < HPW; ++h) LB[h] = 0.f;
             }
-            if (tt == 0 && it + p.grid < p.n_items) {
-                if (!gqa_qlimbs<G, NK, NV>(p, smem, it + p.grid, (kq + 1) & 1, use, sEn)) return;
+            if (tt == 0) {
+                const int nxt = next_item(p, it + p.grid);
+                if (nxt < p.n_items && !gqa_qlimbs<G, NK, NV>(p, smem, nxt, (kq + 1) & 1, use, sEn)) return;
             }
 #pragma unroll
             for (int h = 0; h < HPW; ++h) { mA[h] = m[h]; FA[h] = FB[h]; LA[h] = LB[h]; }
@@ -687,7 +712,7 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV>::THREADS, MINB) gqa_tc_kerne
     constexpr int EW = 4 * C::NWG;  // epilogue warps; then the producer warp, then the MMA warp
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    if (static_cast<int>(blockIdx.x) >= p.n_items) return;
+    if (next_item(p, blockIdx.x) >= p.n_items) return;  // no (non-empty) item for this CTA
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     uint64_t* done = bars + C::B_DONE;
@@ -741,6 +766,70 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV>::THREADS, MINB) gqa_tc_kerne
 }
 
 }  // namespace kvd
+
+// Ragged batches: sequences sorted by length, longest first (one block,
+// bitonic sort of (length, index) keys; B <= 4096).
+__global__ void __launch_bounds__(1024) seq_order_kernel(const int32_t* seq_lens, int B, int S, int32_t* order) {
+    __shared__ unsigned long long keys[4096];
+    int n2 = 1;
+    while (n2 < B) n2 <<= 1;
+    for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+        unsigned long long k = ~0ull;
+        if (i < B) {
+            const int len = min(max(0, seq_lens[i]), S);
+            k = (static_cast<unsigned long long>(0x7FFFFFFF - len) << 32) | static_cast<unsigned>(i);
+        }
+        keys[i] = k;
+    }
+    __syncthreads();
+    for (int k = 2; k <= n2; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const bool asc = (i & k) == 0;
+                    const unsigned long long a = keys[i], b = keys[ixj];
+                    if ((a > b) == asc) { keys[i] = b; keys[ixj] = a; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (int i = threadIdx.x; i < B; i += blockDim.x) order[i] = static_cast<int32_t>(keys[i] & 0xffffffffu);
+}
+
+// Ragged batches: merge the split records of rows whose sequence had more
+// than one split (single-split rows were written by the decode kernel).
+__global__ void __launch_bounds__(128) gqa_ragged_combine_kernel(const float* partials, const int32_t* seq_lens,
+                                                                 int Hq, int P, int span, int S, int D, float* out,
+                                                                 int64_t o_sb, int64_t o_sh, uint32_t flags) {
+    const int64_t r = blockIdx.x;
+    const int b = static_cast<int>(r / Hq), hq = static_cast<int>(r - static_cast<int64_t>(b) * Hq);
+    const int len = min(max(0, seq_lens[b]), S);
+    const int ns = len > 0 ? (len + span - 1) / span : 1;
+    if (ns <= 1) return;
+    const float* first = partials + r * P * static_cast<int64_t>(D + 4);
+    float M = -INFINITY;
+    for (int k = 0; k < ns; ++k) M = fmaxf(M, first[k * (D + 4)]);
+    float* row = out + b * o_sb + static_cast<int64_t>(hq) * o_sh;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float O = 0.f, L = 0.f;
+        if (M != -INFINITY) {
+            for (int k = 0; k < ns; ++k) {
+                const float* rec = first + k * (D + 4);
+                const float f = exp2f(rec[0] - M);
+                O = fmaf(f, rec[4 + d], O);
+                L = fmaf(f, rec[1], L);
+            }
+        }
+        if (flags & KVD_FLAG_PARTIAL_OUT) {
+            if (d == 0) { row[0] = M; row[1] = L; }
+            row[4 + d] = O;
+        } else {
+            row[d] = L > 0.f ? O / L : 0.f;
+        }
+    }
+}
 
 // ------------------------------------------------------------------ host side
 namespace kvd {
@@ -831,37 +920,67 @@ bool gqa_path_ok(const kvd_decode_desc& d) {
     return tensor_map_encoder() != nullptr;
 }
 
+namespace {
+// Work plan of one launch: token span per item, splits per sequence, and the
+// workspace it needs (ragged order array, split records).
+struct GqaPlan {
+    int P, span;
+    size_t order_bytes, rec_bytes;
+};
+
+GqaPlan plan_gqa(const kvd_decode_desc& d, size_t ws_limit) {
+    GqaPlan g{};
+    const int S = d.max_seq_len > 0 ? d.max_seq_len : 1;
+    const int64_t units = static_cast<int64_t>(d.batch) * d.num_kv_heads;
+    const int64_t grid = static_cast<int64_t>(device_sm_count()) * kGqaCtas;
+    const int s_tiles = (S + 127) / 128;
+    g.order_bytes = (d.seq_lens && d.batch <= 4096) ? ((static_cast<size_t>(d.batch) * 4 + 255) & ~size_t(255)) : 0;
+    int span_tiles;
+    if (d.seq_lens) {
+        // Ragged: split long sequences into items of at most 16 tiles (fewer if
+        // that leaves too few items to balance), longest items dealt first.
+        span_tiles = 16;
+        while (span_tiles > 1 && units * ((s_tiles + span_tiles - 1) / span_tiles) < 4 * grid) span_tiles /= 2;
+        if (span_tiles > s_tiles) span_tiles = s_tiles;
+    } else {
+        const int P0 = gqa_split_count(d);
+        span_tiles = (s_tiles + P0 - 1) / P0;
+    }
+    g.span = 128 * span_tiles;
+    g.P = (S + g.span - 1) / g.span;
+    g.rec_bytes = g.P > 1 ? static_cast<size_t>(d.batch) * d.num_q_heads * g.P * (d.head_dim + 4) * sizeof(float) : 0;
+    if (g.order_bytes + g.rec_bytes > ws_limit) {  // no room for split records: whole sequences per item
+        g.span = 128 * s_tiles;
+        g.P = 1;
+        g.rec_bytes = 0;
+        if (g.order_bytes > ws_limit) g.order_bytes = 0;
+    }
+    return g;
+}
+}  // namespace
+
 size_t gqa_workspace_size(const kvd_decode_desc& d) {
-    const int P = gqa_split_count(d);
-    if (P <= 1) return 0;
-    return static_cast<size_t>(d.batch) * d.num_q_heads * P * (d.head_dim + 4) * sizeof(float);
+    const GqaPlan g = plan_gqa(d, ~size_t(0));
+    return g.order_bytes + g.rec_bytes;
 }
 
 cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const float* Q, const int8_t* K, const int8_t* V,
                           const float* ks, const float* vs, float* out, void* ws, size_t ws_bytes,
                           cudaStream_t st, int* launches) {
     const int G = d.num_q_heads / d.num_kv_heads;
-    const int64_t rec_row_bytes = static_cast<int64_t>(d.batch) * d.num_q_heads * (d.head_dim + 4) * 4;
-    int P = gqa_split_count(d);
-    if (P > 1) {
-        const int64_t fit = ws ? static_cast<int64_t>(ws_bytes) / rec_row_bytes : 0;
-        if (fit < P) P = static_cast<int>(fit);
-        if (P < 2) P = 1;
-    }
+    const GqaPlan g = plan_gqa(d, ws ? ws_bytes : 0);
     const int S = d.max_seq_len;
-    const int span = ((((S + P - 1) / P) + 127) / 128) * 128;
-    P = (S + span - 1) / span;
-    if (P < 1) P = 1;
     CUtensorMap km, vm;
     if (!make_kv_map(&km, K, d.batch, d.num_kv_heads, S, d.kv_stride_b, d.kv_stride_h) ||
         !make_kv_map(&vm, V, d.batch, d.num_kv_heads, S, d.kv_stride_b, d.kv_stride_h))
         return cudaErrorInvalidValue;
     GqaParams p{};
     p.Q = Q; p.ks = ks; p.vs = vs; p.out = out;
-    p.partials = P > 1 ? static_cast<float*>(ws) : nullptr;
+    p.order = g.order_bytes ? static_cast<const int32_t*>(ws) : nullptr;
+    p.partials = g.rec_bytes ? reinterpret_cast<float*>(static_cast<char*>(ws) + g.order_bytes) : nullptr;
     p.seq_lens = d.seq_lens;
-    p.B = d.batch; p.Hq = d.num_q_heads; p.Hkv = d.num_kv_heads; p.S = S; p.P = P; p.span = span;
-    p.n_items = d.batch * d.num_kv_heads * P;
+    p.B = d.batch; p.Hq = d.num_q_heads; p.Hkv = d.num_kv_heads; p.S = S; p.P = g.P; p.span = g.span;
+    p.n_items = d.batch * d.num_kv_heads * g.P;
     const int64_t grid_max = static_cast<int64_t>(device_sm_count()) * kGqaCtas;
     p.grid = static_cast<int>(grid_max < p.n_items ? grid_max : p.n_items);
     p.sc_sb = d.sc_stride_b; p.sc_sh = d.sc_stride_h;
@@ -871,6 +990,12 @@ cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const float* Q, const int8_t
     p.qscale = scale * 1.4426950408889634f;
     p.flags = d.flags;
     cudaError_t e;
+    if (p.order) {
+        seq_order_kernel<<<1, 1024, 0, st>>>(d.seq_lens, d.batch, S, static_cast<int32_t*>(ws));
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        ++*launches;
+    }
     switch (G) {
         case 1: e = launch_gqa_g<1>(km, vm, p, st); break;
         case 2: e = launch_gqa_g<2>(km, vm, p, st); break;
@@ -881,11 +1006,19 @@ cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const float* Q, const int8_t
     }
     if (e != cudaSuccess) return e;
     ++*launches;
-    if (P > 1) {
-        const int64_t rs = d.head_dim + 4;
-        e = launch_combine_records(static_cast<const float*>(ws), P, rs, rs * P,
-                                   static_cast<int64_t>(d.batch) * d.num_q_heads, d.num_q_heads, d.head_dim, out,
-                                   d.o_stride_b, d.o_stride_h, d.flags, st, launches);
+    if (g.P > 1) {
+        const int64_t rows = static_cast<int64_t>(d.batch) * d.num_q_heads;
+        if (d.seq_lens) {
+            gqa_ragged_combine_kernel<<<static_cast<unsigned>(rows), 128, 0, st>>>(
+                p.partials, d.seq_lens, d.num_q_heads, g.P, g.span, S, d.head_dim, out, d.o_stride_b, d.o_stride_h,
+                d.flags);
+            e = cudaGetLastError();
+            if (e == cudaSuccess) ++*launches;
+        } else {
+            const int64_t rs = d.head_dim + 4;
+            e = launch_combine_records(p.partials, g.P, rs, rs * g.P, rows, d.num_q_heads, d.head_dim, out,
+                                       d.o_stride_b, d.o_stride_h, d.flags, st, launches);
+        }
     }
     return e;
 }
