@@ -101,3 +101,50 @@ def test_sequence_split_orchestration_on_two_gloo_ranks():
         assert p.exitcode == 0
     assert set(result.keys()) == {0, 1}
     assert max(result.values()) < 1e-5  # fp32 records, fp64 combine
+
+
+def _dropout_rank(rank, world, port, result):
+    import datetime
+    import sys
+
+    import torch
+    import torch.distributed as dist
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [os.path.join(root, "cuda-operators_b200"), os.path.join(root, "oracle")]
+    import kvd_mgpu
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        result[1] = "left before the collective"
+        os._exit(0)  # the rank disappears between steps, with nothing in flight
+    dec = kvd_mgpu.SeqSplitDecode(1, 2, 8, "cpu", local_decode=lambda *a: None, combine=lambda parts, out: None)
+    try:
+        dec(torch.zeros(1, 2, 8), None, None, None, None)
+        result[0] = "no error"
+    except Exception as exc:  # the survivor must learn of it instead of hanging
+        result[0] = f"error: {type(exc).__name__}"
+    os._exit(0)
+
+
+def test_rank_that_leaves_turns_into_an_error_not_a_hang():
+    import time
+
+    import torch.multiprocessing as tmp
+
+    ctx = tmp.get_context("spawn")
+    mgr = ctx.Manager()
+    result = mgr.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_dropout_rank, args=(r, 2, port, result)) for r in range(2)]
+    t0 = time.time()
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(90)
+        if p.is_alive():
+            p.kill()
+    assert time.time() - t0 < 90
+    assert result.get(1) == "left before the collective"
+    assert str(result.get(0, "")).startswith("error"), result.get(0)
