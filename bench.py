@@ -207,6 +207,37 @@ def run_reference(args) -> None:
 
 
 # ---------------------------------------------------------------- GPU leg
+def to_paged_pool(case, bs: int, Hkv: int, D: int, seed: int, dev):
+    """Moves the case's dense cache into block pools [blocks, Hkv, bs, D] in a
+    seeded random block order; returns the pools, the block table and the
+    lengths (every sequence at its dense length when the case is not ragged)."""
+    import torch
+
+    B, _, cap, _ = case.K.shape
+    nb = -(-cap // bs)
+    pad = nb * bs - cap
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    table = torch.randperm(B * nb, generator=g).to(torch.int32).view(B, nb).to(dev)
+    idx = table.flatten().long()
+    pool = {"table": table}
+    for name in ("K", "V", "ks", "vs"):
+        x = getattr(case, name)
+        if pad:
+            x = torch.nn.functional.pad(x, ((0, 0, 0, pad) if x.dim() == 4 else (0, pad)))
+        if x.dim() == 4:
+            blocks = x.view(B, Hkv, nb, bs, D).permute(0, 2, 1, 3, 4).reshape(B * nb, Hkv, bs, D)
+        else:
+            blocks = x.view(B, Hkv, nb, bs).permute(0, 2, 1, 3).reshape(B * nb, Hkv, bs)
+        p = torch.empty_like(blocks)
+        p[idx] = blocks
+        pool[name] = p
+        setattr(case, name, None)  # free the dense copy
+    pool["lens"] = (case.seq_lens.clone() if case.seq_lens is not None
+                    else torch.full((B,), cap, dtype=torch.int32, device=dev))
+    torch.cuda.synchronize()
+    return pool
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -248,13 +279,27 @@ def run_ours(args) -> None:
     if not seqsplit:
         nbytes = wl.step_bytes(cfg, lens_final if cfg.ragged else None, batch=B)
         job_bytes = nbytes * world
-    desc = kvd.make_desc(case.q, case.K, case.ks, out, case.seq_lens)
-    ws = torch.empty(max(kvd.workspace_size(desc), 1), dtype=torch.uint8, device=dev)
+    if args.paged and not seqsplit:
+        pool = to_paged_pool(case, args.paged, cfg.kv_heads, cfg.head_dim, args.seed, dev)
+        pdesc = kvd.make_paged_desc(case.q, pool["K"], pool["ks"], out, pool["table"], pool["lens"])
+        ws = torch.empty(max(kvd.paged_workspace_size(pdesc), 1), dtype=torch.uint8, device=dev)
+    else:
+        pool = None
+        desc = kvd.make_desc(case.q, case.K, case.ks, out, case.seq_lens)
+        ws = torch.empty(max(kvd.workspace_size(desc), 1), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
 
     def step():  # launches on the current stream (a capture stream while a graph is recorded)
         if seqsplit:
             splitter(case.q, case.K, case.V, case.ks, case.vs, out=out)
+            return
+        if pool is not None:
+            if cfg.append:
+                pool["lens"].copy_(lens0)
+                kvd.paged_append(case.k_new, case.v_new, pool["K"], pool["V"], pool["ks"], pool["vs"],
+                                 pool["table"], pool["lens"])
+            kvd.paged_decode(case.q, pool["K"], pool["V"], pool["ks"], pool["vs"], pool["table"], pool["lens"],
+                             out=out, workspace=ws)
             return
         if cfg.append:
             case.seq_lens.copy_(lens0)
@@ -310,7 +355,7 @@ def run_ours(args) -> None:
     # ---- end to end through the reference-facing C ABI with host buffers
     q_host = case.q.cpu().pin_memory()
     out_host = torch.empty(out.shape, dtype=torch.float32).pin_memory()
-    flat = not cfg.ragged and cfg.q_heads == cfg.kv_heads and not seqsplit
+    flat = not cfg.ragged and cfg.q_heads == cfg.kv_heads and not seqsplit and pool is None
     if flat:
         H = B * cfg.q_heads
         scratch = torch.empty(H * cfg.seq_len, dtype=torch.float32, device=dev)
@@ -343,7 +388,8 @@ def run_ours(args) -> None:
         "data": "synthetic: seeded N(0,1) Q/K/V (torch Philox on device), K/V quantised per token by the library",
         "config": {
             "workload": (f"config{args.config} {cfg.name}: B={B}/GPU Hq={cfg.q_heads} Hkv={cfg.kv_heads} "
-                         f"D={cfg.head_dim} S={cfg.seq_len}" + (" ragged+append" if cfg.ragged else "")),
+                         f"D={cfg.head_dim} S={cfg.seq_len}" + (" ragged+append" if cfg.ragged else "")
+                         + (f" paged cache, {args.paged}-token blocks in random pool order" if pool else "")),
             "global_batch": B if seqsplit else B * world, "seq_len": cfg.seq_len,
             "parallelism": (f"sequence split x{world}, NCCL all-gather of (m, l, o) records + LSE combine"
                             if seqsplit else f"batch shards x{world}, no comm"),
@@ -359,7 +405,8 @@ def run_ours(args) -> None:
         "clocks": clk.summary(),
         "e2e": {"value": e2e_gbs, "unit": "GB/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": int(q_host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4),
-                "call": "kv_int8_split_launch" if flat else "kvd_decode_launch"},
+                "call": ("kv_int8_split_launch" if flat else
+                         "kvd_paged_decode_launch" if pool is not None else "kvd_decode_launch")},
         "gpu_launches": launches_per_step * args.steps,
         "launch": f"CUDA graph of {G} steps" if G > 1 else "direct launches",
     }
@@ -385,6 +432,8 @@ def main() -> None:
     ap.add_argument("--cpu-heads", type=int, default=512, help="query heads in the CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every step directly instead of from a CUDA graph")
+    ap.add_argument("--paged", type=int, default=0, metavar="BS",
+                    help="decode through the paged-cache entry point with BS-token blocks (0: dense cache)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -152,6 +152,104 @@ extern "C" cudaError_t kvd_decode_launch(const kvd_decode_desc* desc, const floa
     return launch_splitkv(p, stream, &tl_launches);
 }
 
+namespace {
+cudaError_t check_paged(const kvd_paged_desc* d) {
+    if (d == nullptr || !d->seq_lens || !d->block_table) return cudaErrorInvalidValue;
+    if (d->batch < 1 || d->num_q_heads < 1 || d->num_kv_heads < 1 || d->head_dim < 1) return cudaErrorInvalidValue;
+    if (d->num_q_heads % d->num_kv_heads != 0) return cudaErrorInvalidValue;
+    if (d->block_size < 1 || d->num_blocks < 1 || d->max_blocks_per_seq < 1) return cudaErrorInvalidValue;
+    if (d->block_table_stride < d->max_blocks_per_seq) return cudaErrorInvalidValue;
+    if (static_cast<int64_t>(d->max_blocks_per_seq) * d->block_size > 0x7fffffffLL) return cudaErrorInvalidValue;
+    if ((d->flags & ~KVD_FLAG_PARTIAL_OUT) != 0) return cudaErrorInvalidValue;
+    return cudaSuccess;
+}
+
+// The dense descriptor the planners see: ragged lengths over a capacity of
+// max_blocks_per_seq * block_size tokens; the pool addressing rides in a PagedView.
+kvd_decode_desc paged_as_dense(const kvd_paged_desc& p, PagedView* pv) {
+    kvd_decode_desc d{};
+    d.batch = p.batch; d.num_q_heads = p.num_q_heads; d.num_kv_heads = p.num_kv_heads; d.head_dim = p.head_dim;
+    d.max_seq_len = p.max_blocks_per_seq * p.block_size;
+    d.flags = p.flags;
+    d.seq_lens = p.seq_lens;
+    d.kv_stride_b = 0; d.kv_stride_h = p.kv_stride_h;
+    d.sc_stride_b = 0; d.sc_stride_h = p.sc_stride_h;
+    d.q_stride_b = p.q_stride_b; d.q_stride_h = p.q_stride_h;
+    d.o_stride_b = p.o_stride_b; d.o_stride_h = p.o_stride_h;
+    d.softmax_scale = p.softmax_scale;
+    pv->table = p.block_table;
+    pv->bt_stride = p.block_table_stride;
+    pv->block_size = p.block_size;
+    pv->num_blocks = p.num_blocks;
+    pv->kv_sblk = p.kv_stride_block;
+    pv->kv_st = p.kv_stride_t;
+    pv->sc_sblk = p.sc_stride_block;
+    return d;
+}
+
+bool paged_tc_shape(const kvd_paged_desc& p, const kvd_decode_desc& d) {
+    const int bs = p.block_size;
+    return bs >= 8 && (bs & (bs - 1)) == 0 && gqa_path_ok(d);
+}
+
+bool paged_tc_ok(const kvd_paged_desc& p, const kvd_decode_desc& d, const float* Q, const int8_t* K,
+                 const int8_t* V, const float* ks, const float* vs) {
+    if (!paged_tc_shape(p, d)) return false;
+    if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(ks) || !aligned16(vs)) return false;
+    if (((p.kv_stride_block | p.kv_stride_h | p.kv_stride_t) & 15) != 0) return false;
+    if (p.kv_stride_block <= 0 || p.kv_stride_h <= 0 || p.kv_stride_t <= 0) return false;
+    if (((p.sc_stride_block | p.sc_stride_h) & 3) != 0) return false;
+    if (((p.q_stride_b | p.q_stride_h) & 3) != 0) return false;
+    return true;
+}
+}  // namespace
+
+extern "C" size_t kvd_paged_workspace_size(const kvd_paged_desc* desc) {
+    if (check_paged(desc) != cudaSuccess) return 0;
+    PagedView pv;
+    const kvd_decode_desc d = paged_as_dense(*desc, &pv);
+    const size_t gen = generic_workspace_size(d);
+    const size_t gqa = paged_tc_shape(*desc, d) ? gqa_workspace_size(d) : 0;
+    return gen > gqa ? gen : gqa;
+}
+
+extern "C" cudaError_t kvd_paged_decode_launch(const kvd_paged_desc* desc, const float* Q, const int8_t* K_pool,
+                                               const int8_t* V_pool, const float* k_scale_pool,
+                                               const float* v_scale_pool, float* out, void* workspace,
+                                               size_t workspace_bytes, cudaStream_t stream) {
+    tl_launches = 0;
+    cudaError_t e = check_paged(desc);
+    if (e != cudaSuccess) return e;
+    if (!Q || !K_pool || !V_pool || !k_scale_pool || !v_scale_pool || !out) return cudaErrorInvalidValue;
+    if ((desc->flags & KVD_FLAG_PARTIAL_OUT) && desc->num_q_heads > 1 && desc->o_stride_h < desc->head_dim + 4)
+        return cudaErrorInvalidValue;
+    if (!workspace) workspace_bytes = 0;
+    PagedView pv;
+    const kvd_decode_desc d = paged_as_dense(*desc, &pv);
+    if (paged_tc_ok(*desc, d, Q, K_pool, V_pool, k_scale_pool, v_scale_pool))
+        return launch_gqa_tc(d, Q, K_pool, V_pool, k_scale_pool, v_scale_pool, out, workspace, workspace_bytes,
+                             stream, &tl_launches, &pv);
+    return launch_generic(d, Q, K_pool, V_pool, k_scale_pool, v_scale_pool, out, workspace, workspace_bytes, stream,
+                          &tl_launches, &pv);
+}
+
+extern "C" cudaError_t kvd_paged_append_int8_launch(const kvd_paged_desc* desc, const float* k_new,
+                                                    const float* v_new, int64_t new_stride_b, int64_t new_stride_h,
+                                                    int8_t* K_pool, int8_t* V_pool, float* k_scale_pool,
+                                                    float* v_scale_pool, int32_t* seq_lens, cudaStream_t stream) {
+    tl_launches = 0;
+    if (!desc || !desc->block_table || !k_new || !v_new || !K_pool || !V_pool || !k_scale_pool || !v_scale_pool ||
+        !seq_lens)
+        return cudaErrorInvalidValue;
+    if (desc->batch < 1 || desc->num_kv_heads < 1 || desc->head_dim < 1 || desc->block_size < 1 ||
+        desc->num_blocks < 1 || desc->max_blocks_per_seq < 1 || desc->block_table_stride < desc->max_blocks_per_seq)
+        return cudaErrorInvalidValue;
+    const cudaError_t e = launch_paged_append(*desc, k_new, v_new, new_stride_b, new_stride_h, K_pool, V_pool,
+                                              k_scale_pool, v_scale_pool, seq_lens, stream);
+    if (e == cudaSuccess) tl_launches = 1;
+    return e;
+}
+
 extern "C" cudaError_t kvd_combine_launch(const float* parts, int num_parts, int64_t part_stride, int num_heads,
                                           int head_dim, float* out, int64_t out_stride, uint32_t flags,
                                           cudaStream_t stream) {

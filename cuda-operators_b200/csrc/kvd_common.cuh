@@ -1,6 +1,6 @@
 // kvd_common.cuh -- device helpers shared by the sm_100a decode kernels:
 // mbarriers with bounded waits, 1-D bulk async copies (TMA engine, no tensor
-// map, no multicast), packed fp32x2 arithmetic and the exact INT8 -> fp32
+// map, CTA-local destinations only), packed fp32x2 arithmetic and the exact INT8 -> fp32
 // conversion used on the CUDA-core path.
 #pragma once
 
@@ -47,6 +47,14 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;"
                  ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// Raises the pending transaction count of the current phase without
+// arriving (for copies whose number is only known while they are issued;
+// the issuer arrives once after the last one).
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {

@@ -75,6 +75,18 @@ constexpr int sk_ctas_per_sm(int D) { return D == 64 ? KVD_SK64_CTAS : KVD_SK128
 // Tokens per tile of the CUDA-core kernel for a head dimension.
 constexpr int tile_tokens(int D) { return sk_consumer_warps(D) * (32 / (D / 16)) * 4; }
 
+// Paged-cache addressing handed to the launchers next to a descriptor whose
+// max_seq_len is the table's capacity (max_blocks_per_seq * block_size).
+// Token t of sequence b, kv head h: block table[b*bt_stride + t/block_size],
+// codes at blk*kv_sblk + h*kv_sh + (t%block_size)*kv_st, scales at
+// blk*sc_sblk + h*sc_sh + t%block_size.
+struct PagedView {
+    const int32_t* table;
+    int64_t bt_stride;
+    int block_size, num_blocks;
+    int64_t kv_sblk, kv_st, sc_sblk;
+};
+
 bool fast_path_ok(const kvd_decode_desc& d, const float* Q, const int8_t* K, const int8_t* V);
 
 // Per-device cached properties.
@@ -86,7 +98,8 @@ cudaError_t launch_plan(const int32_t* seq_lens, int B, int Hq, int tok, int cap
 cudaError_t launch_splitkv(const DecodeParams& p, cudaStream_t st, int* launches);
 cudaError_t launch_generic(const kvd_decode_desc& d, const float* Q, const int8_t* K,
                            const int8_t* V, const float* ks, const float* vs, float* out,
-                           void* ws, size_t ws_bytes, cudaStream_t st, int* launches);
+                           void* ws, size_t ws_bytes, cudaStream_t st, int* launches,
+                           const PagedView* pv = nullptr);
 size_t generic_workspace_size(const kvd_decode_desc& d);
 cudaError_t launch_combine_records(const float* base, int nparts, int64_t part_stride, int64_t rec_stride,
                                    int64_t rows, int rows_per_b, int D, float* out, int64_t o_sb, int64_t o_sh,
@@ -95,7 +108,10 @@ bool gqa_path_ok(const kvd_decode_desc& d);
 size_t gqa_workspace_size(const kvd_decode_desc& d);
 cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const float* Q, const int8_t* K, const int8_t* V,
                           const float* ks, const float* vs, float* out, void* ws, size_t ws_bytes,
-                          cudaStream_t st, int* launches);
+                          cudaStream_t st, int* launches, const PagedView* pv = nullptr);
+cudaError_t launch_paged_append(const kvd_paged_desc& d, const float* k_new, const float* v_new, int64_t new_sb,
+                                int64_t new_sh, int8_t* K, int8_t* V, float* ks, float* vs, int32_t* seq_lens,
+                                cudaStream_t st);
 cudaError_t launch_combine_parts(const float* parts, int num_parts, int64_t part_stride, int num_heads,
                                  int head_dim, float* out, int64_t out_stride, uint32_t flags,
                                  cudaStream_t st, int* launches);

@@ -29,12 +29,37 @@ struct GenParams {
     int64_t kv_sb, kv_sh, sc_sb, sc_sh, q_sb, q_sh, o_sb, o_sh;
     float qscale;
     uint32_t flags;
+    PagedView pv;  // pv.table == nullptr: dense cache
 };
+
+// Code row offset and scale offset of token t of (b, kv head hk). A paged
+// block id outside the pool reads block 0 with both scales forced to 0 (score
+// 0, weight 0) and records KVD_STATUS_BAD_BLOCK.
+__device__ __forceinline__ void token_offsets(const GenParams& p, int b, int hk, int t, int64_t& row, int64_t& sc,
+                                              bool& ok) {
+    ok = true;
+    if (!p.pv.table) {
+        row = b * p.kv_sb + static_cast<int64_t>(hk) * p.kv_sh + static_cast<int64_t>(t) * p.D;
+        sc = b * p.sc_sb + static_cast<int64_t>(hk) * p.sc_sh + t;
+        return;
+    }
+    const int j = t / p.pv.block_size, off = t - j * p.pv.block_size;
+    int blk = p.pv.table[b * p.pv.bt_stride + j];
+    if (blk < 0 || blk >= p.pv.num_blocks) {
+        record_status(KVD_STATUS_BAD_BLOCK);
+        blk = 0;
+        ok = false;
+    }
+    row = blk * p.pv.kv_sblk + static_cast<int64_t>(hk) * p.kv_sh + static_cast<int64_t>(off) * p.pv.kv_st;
+    sc = blk * p.pv.sc_sblk + static_cast<int64_t>(hk) * p.sc_sh + off;
+}
 
 __global__ void __launch_bounds__(kGenThreads) generic_decode_kernel(const GenParams p) {
     __shared__ float qs[kGenMaxD];
     __shared__ float sc[kGenChunk];
     __shared__ float wt[kGenChunk];
+    __shared__ int64_t rowoff[kGenChunk];
+    __shared__ float kscl[kGenChunk], vscl[kGenChunk];
     const int64_t u = blockIdx.x;
     const int split = blockIdx.y;
     const int b = static_cast<int>(u / p.Hq), hq = static_cast<int>(u % p.Hq);
@@ -44,24 +69,28 @@ __global__ void __launch_bounds__(kGenThreads) generic_decode_kernel(const GenPa
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* q = p.Q + b * p.q_sb + static_cast<int64_t>(hq) * p.q_sh;
     for (int d = tid; d < p.D; d += kGenThreads) qs[d] = q[d] * p.qscale;
-    const int8_t* kh = p.K + b * p.kv_sb + static_cast<int64_t>(hk) * p.kv_sh;
-    const int8_t* vh = p.V + b * p.kv_sb + static_cast<int64_t>(hk) * p.kv_sh;
-    const float* ksh = p.ks + b * p.sc_sb + static_cast<int64_t>(hk) * p.sc_sh;
-    const float* vsh = p.vs + b * p.sc_sb + static_cast<int64_t>(hk) * p.sc_sh;
     float acc[kGenDPT];
 #pragma unroll
     for (int j = 0; j < kGenDPT; ++j) acc[j] = 0.f;
     float m = -INFINITY, l = 0.f;
-    __syncthreads();
     for (int c0 = t_lo; c0 < t_hi; c0 += kGenChunk) {
         const int n = min(kGenChunk, t_hi - c0);
+        if (tid < n) {
+            int64_t row, so;
+            bool ok;
+            token_offsets(p, b, hk, c0 + tid, row, so, ok);
+            rowoff[tid] = row;
+            kscl[tid] = ok ? p.ks[so] : 0.f;
+            vscl[tid] = ok ? p.vs[so] : 0.f;
+        }
+        __syncthreads();
         for (int t = warp; t < n; t += kGenThreads / 32) {
-            const int8_t* kr = kh + static_cast<int64_t>(c0 + t) * p.D;
+            const int8_t* kr = p.K + rowoff[t];
             float dot = 0.f;
             for (int d = lane; d < p.D; d += 32) dot = fmaf(qs[d], static_cast<float>(kr[d]), dot);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-            if (lane == 0) sc[t] = dot * ksh[c0 + t];
+            if (lane == 0) sc[t] = dot * kscl[t];
         }
         __syncthreads();
         float cm = -INFINITY;
@@ -71,7 +100,7 @@ __global__ void __launch_bounds__(kGenThreads) generic_decode_kernel(const GenPa
         if (tid < n) {
             const float pr = exp2f(sc[tid] - m_new);
             sc[tid] = pr;
-            wt[tid] = pr * vsh[c0 + tid];
+            wt[tid] = pr * vscl[tid];
         }
         __syncthreads();
         float ps = 0.f;
@@ -83,7 +112,7 @@ __global__ void __launch_bounds__(kGenThreads) generic_decode_kernel(const GenPa
             if (d < p.D) {
                 float a = acc[j] * alpha;
                 for (int t = 0; t < n; ++t)
-                    a = fmaf(wt[t], static_cast<float>(vh[static_cast<int64_t>(c0 + t) * p.D + d]), a);
+                    a = fmaf(wt[t], static_cast<float>(p.V[rowoff[t] + d]), a);
                 acc[j] = a;
             }
         }
@@ -163,7 +192,7 @@ size_t generic_workspace_size(const kvd_decode_desc& d) {
 
 cudaError_t launch_generic(const kvd_decode_desc& d, const float* Q, const int8_t* K,
                            const int8_t* V, const float* ks, const float* vs, float* out,
-                           void* ws, size_t ws_bytes, cudaStream_t st, int* launches) {
+                           void* ws, size_t ws_bytes, cudaStream_t st, int* launches, const PagedView* pv) {
     if (d.head_dim > kGenMaxD) return cudaErrorInvalidValue;
     const int64_t units = static_cast<int64_t>(d.batch) * d.num_q_heads;
     int splits = generic_splits(d, device_sm_count());
@@ -190,6 +219,7 @@ cudaError_t launch_generic(const kvd_decode_desc& d, const float* Q, const int8_
     const float scale = d.softmax_scale > 0.f ? d.softmax_scale : 1.0f / sqrtf(static_cast<float>(d.head_dim));
     p.qscale = scale * 1.4426950408889634f;
     p.flags = d.flags;
+    p.pv = pv ? *pv : PagedView{};
     generic_decode_kernel<<<dim3(static_cast<unsigned>(units), splits), kGenThreads, 0, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;

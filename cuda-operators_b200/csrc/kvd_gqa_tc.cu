@@ -51,6 +51,11 @@ struct GqaParams {
     int64_t sc_sb, sc_sh, q_sb, q_sh, o_sb, o_sh;
     float qscale;
     uint32_t flags;
+    // Paged cache (table != nullptr): the maps view the pools as
+    // {D, block_size, Hkv, num_blocks}; lbs = log2(block_size) >= 3.
+    const int32_t* table;
+    int64_t bt_stride, sc_sblk;
+    int lbs, nblk;
 };
 
 template <int G, int NK_, int NV_>
@@ -264,6 +269,157 @@ struct __align__(16) GMeta {
 };
 
 // ------------------------------------------------------------------ producer
+// Paged cache: the whole producer warp issues the copies of a tile, one box
+// of min(block_size, 128) token rows per block (a tile never straddles a
+// block when block_size >= 128; at most 16 boxes per tile, block_size >= 8),
+// so a tile of small blocks costs one warp-wide issue instead of many serial
+// ones. Lane j < 16 owns box j (its K box and V box). Scales: for blocks of
+// 128 tokens or more, two bulk copies per tile (lanes 0 and 16); for smaller
+// blocks, which would need two tiny copies per block, lane l loads the scales
+// of tokens 4l..4l+3 with one 16-byte load per pool and stores them into the
+// slot. Table reads run two tiles ahead and scale loads one tile ahead, so
+// neither latency stalls the issue. Each ring slot is armed once with the
+// sum of the bytes its lanes copy. K runs at most one tile ahead of V here.
+// A block id outside the pool is not read: its scales are zeroed (score 0,
+// weight 0) and the status word records it.
+struct PTile {
+    int it, tt, t0, n;
+    GItem I;
+};
+
+// First tile of this CTA; it = n_items when there is none.
+__device__ __forceinline__ PTile ptile_first(const GqaParams& p) {
+    PTile T;
+    T.it = next_item(p, blockIdx.x);
+    T.tt = 0;
+    T.t0 = 0;
+    T.n = 0;
+    T.I = GItem{0, 0, 0, 0, 0, 0};
+    if (T.it < p.n_items) {
+        T.I = gqa_item(p, T.it);
+        T.t0 = T.I.t_lo;
+        T.n = max(0, min(128, T.I.t_hi - T.t0));
+    }
+    return T;
+}
+
+__device__ __forceinline__ PTile ptile_next(const GqaParams& p, const PTile& A) {
+    PTile T = A;
+    if (T.it >= p.n_items) return T;
+    if (++T.tt >= T.I.ntiles) {
+        T.tt = 0;
+        T.it = next_item(p, T.it + p.grid);
+        if (T.it >= p.n_items) return T;
+        T.I = gqa_item(p, T.it);
+    }
+    T.t0 = T.I.t_lo + T.tt * 128;
+    T.n = max(0, min(128, T.I.t_hi - T.t0));
+    return T;
+}
+
+// Block id of this lane's box (lane & 15) of tile T, -1 past the tile.
+__device__ __forceinline__ int ptile_block(const GqaParams& p, const PTile& T, int rows, int lane) {
+    const int tok = (lane & 15) * rows;
+    if (T.it >= p.n_items || tok >= T.n) return -1;
+    return __ldg(p.table + T.I.b * p.bt_stride + ((T.t0 + tok) >> p.lbs));
+}
+
+// Scales of tokens 4*lane .. 4*lane+3 of tile T (blocks of 8..64 tokens);
+// zero past the tile or in a block outside the pool.
+__device__ __forceinline__ void ptile_scales(const GqaParams& p, const PTile& T, int blk, int lane, float4& kq,
+                                             float4& vq) {
+    const int tl = 4 * lane;
+    const int sblk = __shfl_sync(0xffffffffu, blk, (tl >> p.lbs) & 15);
+    kq = make_float4(0.f, 0.f, 0.f, 0.f);
+    vq = kq;
+    if (T.it < p.n_items && tl < T.n && sblk >= 0 && sblk < p.nblk) {
+        const int64_t so = sblk * p.sc_sblk + T.I.hk * p.sc_sh + ((T.t0 + tl) & ((1 << p.lbs) - 1));
+        kq = __ldcs(reinterpret_cast<const float4*>(p.ks + so));
+        vq = __ldcs(reinterpret_cast<const float4*>(p.vs + so));
+    }
+}
+
+template <int G, int NK, int NV>
+__device__ __forceinline__ void gqa_producer_paged(const CUtensorMap* kmap, const CUtensorMap* vmap,
+                                                   const GqaParams& p, uint8_t* smem) {
+    using C = GqaCfg<G, NK, NV>;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+    GMeta* meta = reinterpret_cast<GMeta*>(smem + C::OFF_META);
+    const uint64_t pol = policy_evict_first();
+    const int lane = threadIdx.x & 31, j = lane & 15;
+    const int bs = 1 << p.lbs;
+    const int rows = bs < C::TOK ? bs : C::TOK;
+    const bool small = rows < C::TOK;
+    const uint32_t box = static_cast<uint32_t>(rows) * C::D;
+    int64_t ik = 0, iv = 0;  // tiles issued on each ring
+    PTile T0 = ptile_first(p);
+    PTile T1 = ptile_next(p, T0);
+    int b0 = ptile_block(p, T0, rows, lane), b1 = ptile_block(p, T1, rows, lane);
+    float4 kq0, vq0;
+    if (small) ptile_scales(p, T0, b0, lane, kq0, vq0);
+    while (T0.it < p.n_items) {
+        const PTile T2 = ptile_next(p, T1);
+        const int b2 = ptile_block(p, T2, rows, lane);  // two tiles ahead
+        float4 kq1, vq1;
+        if (small) ptile_scales(p, T1, b1, lane, kq1, vq1);  // one tile ahead
+        const int tok = j * rows;
+        const bool act = tok < T0.n;
+        const bool good = act && b0 >= 0 && b0 < p.nblk;
+        if (act && !good && lane < 16) record_status(KVD_STATUS_BAD_BLOCK);
+        const int off = (T0.t0 + tok) & (bs - 1);
+        // ---- K slot
+        const int sk = static_cast<int>(ik % NK);
+        if (ik >= NK && !mbar_wait(&bars[C::B_KEMPTY + sk], static_cast<uint32_t>(((ik / NK) - 1) & 1))) break;
+        uint32_t bytes = __reduce_add_sync(0xffffffffu, (lane < 16 && good) ? box : 0u);
+        if (lane == 0) mbar_arrive_expect_tx(&bars[C::B_KFULL + sk], bytes);
+        __syncwarp();
+        if (lane < 16 && good)
+            tma_load_4d(smem + C::OFF_KR + sk * C::TILE_BYTES + tok * C::D, kmap, 0, off, T0.I.hk, b0,
+                        &bars[C::B_KFULL + sk], pol);
+        ++ik;
+        // ---- V slot: V boxes, scales, metadata
+        const int sv = static_cast<int>(iv % NV);
+        if (iv >= NV && !mbar_wait(&bars[C::B_VEMPTY + sv], static_cast<uint32_t>(((iv / NV) - 1) & 1))) break;
+        float* sck = reinterpret_cast<float*>(smem + C::OFF_SC + sv * C::SC_BYTES);
+        const int cnt = act ? min(rows, T0.n - tok) : 0;
+        const uint32_t seg = static_cast<uint32_t>(4 * cnt + 15) & ~15u;  // bulk scale copy (rows == 128)
+        float* dst = lane < 16 ? sck : sck + C::SC_FLOATS;
+        if (small) {
+            reinterpret_cast<float4*>(sck)[lane] = kq0;
+            reinterpret_cast<float4*>(sck + C::SC_FLOATS)[lane] = vq0;
+        } else if (act && !good && (lane & 15) == 0) {
+            for (int x = 0; x < cnt; ++x) dst[x] = 0.f;
+            fence_async_smem();  // order these writes before later bulk copies into the slot
+        }
+        if (lane == 0)
+            meta[sv] = GMeta{T0.it, T0.n, (T0.tt == 0 ? 1 : 0) | (T0.tt == T0.I.ntiles - 1 ? 2 : 0), 0};
+        const uint32_t mine = !good ? 0u : small ? (lane < 16 ? box : 0u) : (lane < 16 ? box + seg : lane == 16 ? seg : 0u);
+        bytes = __reduce_add_sync(0xffffffffu, mine);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(&bars[C::B_VFULL + sv], bytes);
+        __syncwarp();
+        if (good) {
+            const int64_t so = b0 * p.sc_sblk + T0.I.hk * p.sc_sh + off;
+            if (lane < 16)
+                tma_load_4d(smem + C::OFF_VR + sv * C::TILE_BYTES + tok * C::D, vmap, 0, off, T0.I.hk, b0,
+                            &bars[C::B_VFULL + sv], pol);
+            if (!small && lane == 0) bulk_g2s(dst, p.ks + so, seg, &bars[C::B_VFULL + sv], pol);
+            if (!small && lane == 16) bulk_g2s(dst, p.vs + so, seg, &bars[C::B_VFULL + sv], pol);
+        }
+        ++iv;
+        T0 = T1;
+        T1 = T2;
+        b0 = b1;
+        b1 = b2;
+        if (small) { kq0 = kq1; vq0 = vq1; }
+    }
+    // no copy may be in flight when the CTA exits
+    for (int64_t x = ik > NK ? ik - NK : 0; x < ik; ++x)
+        mbar_wait(&bars[C::B_KFULL + x % NK], static_cast<uint32_t>((x / NK) & 1));
+    for (int64_t x = iv > NV ? iv - NV : 0; x < iv; ++x)
+        mbar_wait(&bars[C::B_VFULL + x % NV], static_cast<uint32_t>((x / NV) & 1));
+}
+
 // Lane 0 streams K tiles, lane 1 streams V tiles with both scale windows and
 // the tile metadata; the two rings are released independently (K as soon as
 // QK has read it, V after PV and the softmax), so K loads run ahead of V.
@@ -744,7 +900,8 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV>::THREADS, MINB) gqa_tc_kerne
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + C::OFF_TMEM);
     if (warp == EW) {
-        if (lane < 2) gqa_producer<G, NK, NV>(&kmap, &vmap, p, smem, lane == 1);
+        if (p.table) gqa_producer_paged<G, NK, NV>(&kmap, &vmap, p, smem);
+        else if (lane < 2) gqa_producer<G, NK, NV>(&kmap, &vmap, p, smem, lane == 1);
         return;
     }
     if (warp == EW + 1) {
@@ -870,6 +1027,25 @@ bool make_kv_map(CUtensorMap* m, const int8_t* base, int B, int Hkv, int cap, in
     return r == CUDA_SUCCESS;
 }
 
+// 4-D view {D bytes, block_size tokens, kv heads, blocks} of a paged K or V
+// pool, box of 128 bytes x min(block_size, 128) tokens, 128-byte swizzle. The
+// boxes of one tile land at multiples of 1024 bytes (block_size >= 8), so the
+// tile has the same swizzled layout as a dense 128-token box.
+bool make_paged_map(CUtensorMap* m, const int8_t* base, int Hkv, const PagedView& pv, int64_t kv_sh) {
+    auto fn = tensor_map_encoder();
+    if (!fn) return false;
+    cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(pv.block_size), static_cast<cuuint64_t>(Hkv),
+                          static_cast<cuuint64_t>(pv.num_blocks)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(pv.kv_st), static_cast<cuuint64_t>(kv_sh),
+                             static_cast<cuuint64_t>(pv.kv_sblk)};
+    cuuint32_t box[4] = {128, static_cast<cuuint32_t>(pv.block_size < 128 ? pv.block_size : 128), 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 // Splits per (batch, kv head) item. Items are dealt round-robin to the
 // persistent CTAs, so pick the split count P that minimises
 // rounds(P) * (tiles per item + 1), the +1 standing for the per-item cost
@@ -966,15 +1142,29 @@ size_t gqa_workspace_size(const kvd_decode_desc& d) {
 
 cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const float* Q, const int8_t* K, const int8_t* V,
                           const float* ks, const float* vs, float* out, void* ws, size_t ws_bytes,
-                          cudaStream_t st, int* launches) {
+                          cudaStream_t st, int* launches, const PagedView* pv) {
     const int G = d.num_q_heads / d.num_kv_heads;
     const GqaPlan g = plan_gqa(d, ws ? ws_bytes : 0);
     const int S = d.max_seq_len;
     CUtensorMap km, vm;
-    if (!make_kv_map(&km, K, d.batch, d.num_kv_heads, S, d.kv_stride_b, d.kv_stride_h) ||
-        !make_kv_map(&vm, V, d.batch, d.num_kv_heads, S, d.kv_stride_b, d.kv_stride_h))
+    if (pv) {
+        if (!make_paged_map(&km, K, d.num_kv_heads, *pv, d.kv_stride_h) ||
+            !make_paged_map(&vm, V, d.num_kv_heads, *pv, d.kv_stride_h))
+            return cudaErrorInvalidValue;
+    } else if (!make_kv_map(&km, K, d.batch, d.num_kv_heads, S, d.kv_stride_b, d.kv_stride_h) ||
+               !make_kv_map(&vm, V, d.batch, d.num_kv_heads, S, d.kv_stride_b, d.kv_stride_h)) {
         return cudaErrorInvalidValue;
+    }
     GqaParams p{};
+    if (pv) {
+        p.table = pv->table;
+        p.bt_stride = pv->bt_stride;
+        p.sc_sblk = pv->sc_sblk;
+        p.nblk = pv->num_blocks;
+        int lbs = 0;
+        while ((1 << lbs) < pv->block_size) ++lbs;
+        p.lbs = lbs;
+    }
     p.Q = Q; p.ks = ks; p.vs = vs; p.out = out;
     p.order = g.order_bytes ? static_cast<const int32_t*>(ws) : nullptr;
     p.partials = g.rec_bytes ? reinterpret_cast<float*>(static_cast<char*>(ws) + g.order_bytes) : nullptr;

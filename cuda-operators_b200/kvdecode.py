@@ -27,6 +27,7 @@ KVD_FLAG_PARTIAL_OUT = 1
 KVD_STATUS_OK = 0
 KVD_STATUS_WAIT_TIMEOUT = 1
 KVD_STATUS_CACHE_FULL = 2
+KVD_STATUS_BAD_BLOCK = 4
 CUDA_ERROR_INVALID_VALUE = 1
 
 c_void_p = ctypes.c_void_p
@@ -78,6 +79,34 @@ class AppendDesc(ctypes.Structure):
     ]
 
 
+class PagedDesc(ctypes.Structure):
+    """Mirror of ``kvd_paged_desc``."""
+
+    _fields_ = [
+        ("batch", c_int32),
+        ("num_q_heads", c_int32),
+        ("num_kv_heads", c_int32),
+        ("head_dim", c_int32),
+        ("block_size", c_int32),
+        ("num_blocks", c_int32),
+        ("max_blocks_per_seq", c_int32),
+        ("flags", c_uint32),
+        ("seq_lens", c_void_p),
+        ("block_table", c_void_p),
+        ("block_table_stride", c_int64),
+        ("kv_stride_block", c_int64),
+        ("kv_stride_h", c_int64),
+        ("kv_stride_t", c_int64),
+        ("sc_stride_block", c_int64),
+        ("sc_stride_h", c_int64),
+        ("q_stride_b", c_int64),
+        ("q_stride_h", c_int64),
+        ("o_stride_b", c_int64),
+        ("o_stride_h", c_int64),
+        ("softmax_scale", c_float),
+    ]
+
+
 _SIGNATURES = {
     "solve": (None, [c_void_p] * 6 + [c_int] * 3),
     "kv_int8_split_launch": (c_int, [c_void_p] * 6 + [c_int] * 3 + [c_void_p, c_void_p]),
@@ -92,6 +121,10 @@ _SIGNATURES = {
     "kvd_abi_version": (c_int, []),
     "kvd_error_string": (ctypes.c_char_p, [c_int]),
     "kvd_decode_launch_noalloc": (c_int, [ctypes.POINTER(DecodeDesc)] + [c_void_p] * 6 + [c_void_p]),
+    "kvd_paged_workspace_size": (c_size_t, [ctypes.POINTER(PagedDesc)]),
+    "kvd_paged_decode_launch": (c_int, [ctypes.POINTER(PagedDesc)] + [c_void_p] * 7 + [c_size_t, c_void_p]),
+    "kvd_paged_append_int8_launch": (c_int, [ctypes.POINTER(PagedDesc), c_void_p, c_void_p, c_int64, c_int64]
+                                     + [c_void_p] * 5 + [c_void_p]),
 }
 
 NOALLOC_SCRATCH_BYTES = 512 * 1024
@@ -283,6 +316,81 @@ def quantize_rows(x, codes=None, scales=None, stream=None):
                                         _ptr(scales), _stream(stream))
     _check(rc, "kvd_quantize_rows_launch")
     return codes, scales
+
+
+# ------------------------------------------------------------------ paged cache
+def make_paged_desc(q, k_pool, ks_pool, out, block_table, seq_lens, layout: str = "bhtd",
+                    softmax_scale: float = 0.0, partial: bool = False) -> PagedDesc:
+    """Descriptor for a paged cache. ``k_pool`` is [blocks, Hkv, block_size, D]
+    (layout "bhtd") or [blocks, block_size, Hkv, D] (layout "bthd"); scale pools
+    are [blocks, Hkv, block_size]; ``block_table`` is int32 [B, max_blocks]."""
+    B, Hq, D = q.shape
+    if layout == "bhtd":
+        NB, Hkv, bs, Dk = k_pool.shape
+        s_blk, s_h, s_t = k_pool.stride(0), k_pool.stride(1), k_pool.stride(2)
+    elif layout == "bthd":
+        NB, bs, Hkv, Dk = k_pool.shape
+        s_blk, s_t, s_h = k_pool.stride(0), k_pool.stride(1), k_pool.stride(2)
+    else:
+        raise ValueError(f"unknown pool layout {layout!r}")
+    if Dk != D or Hq % Hkv or tuple(ks_pool.shape) != (NB, Hkv, bs):
+        raise ValueError(f"shape mismatch q{tuple(q.shape)} k_pool{tuple(k_pool.shape)} ks{tuple(ks_pool.shape)}")
+    if k_pool.stride(3) != 1 or ks_pool.stride(2) != 1 or q.stride(2) != 1 or out.stride(2) != 1:
+        raise ValueError("dims and scale tokens must be contiguous")
+    if block_table.dim() != 2 or block_table.shape[0] != B or block_table.stride(1) != 1:
+        raise ValueError("block_table must be int32 [B, max_blocks] with contiguous rows")
+    d = PagedDesc()
+    d.batch, d.num_q_heads, d.num_kv_heads, d.head_dim = B, Hq, Hkv, D
+    d.block_size, d.num_blocks, d.max_blocks_per_seq = bs, NB, block_table.shape[1]
+    d.flags = KVD_FLAG_PARTIAL_OUT if partial else 0
+    d.seq_lens, d.block_table = _ptr(seq_lens), _ptr(block_table)
+    d.block_table_stride = block_table.stride(0)
+    d.kv_stride_block, d.kv_stride_h, d.kv_stride_t = s_blk, s_h, s_t
+    d.sc_stride_block, d.sc_stride_h = ks_pool.stride(0), ks_pool.stride(1)
+    d.q_stride_b, d.q_stride_h = q.stride(0), q.stride(1)
+    d.o_stride_b, d.o_stride_h = out.stride(0), out.stride(1)
+    d.softmax_scale = softmax_scale
+    return d
+
+
+def paged_workspace_size(desc: PagedDesc) -> int:
+    return int(lib().kvd_paged_workspace_size(ctypes.byref(desc)))
+
+
+def paged_decode(q, k_pool, v_pool, ks_pool, vs_pool, block_table, seq_lens, out=None, layout: str = "bhtd",
+                 softmax_scale: float = 0.0, partial: bool = False, workspace=None, stream=None):
+    """INT8 decode attention over a paged cache; returns ``out`` [B,Hq,D] (or records)."""
+    import torch
+
+    B, Hq, D = q.shape
+    if out is None:
+        out = torch.empty((B, Hq, D + 4 if partial else D), dtype=torch.float32, device=q.device)
+    if v_pool.stride() != k_pool.stride() or vs_pool.stride() != ks_pool.stride():
+        raise ValueError("K/V pools and their scale pools must share strides")
+    desc = make_paged_desc(q, k_pool, ks_pool, out, block_table, seq_lens, layout, softmax_scale, partial)
+    if workspace is None:
+        workspace = torch.empty(max(paged_workspace_size(desc), 1), dtype=torch.uint8, device=q.device)
+    rc = lib().kvd_paged_decode_launch(ctypes.byref(desc), _ptr(q), _ptr(k_pool), _ptr(v_pool), _ptr(ks_pool),
+                                       _ptr(vs_pool), _ptr(out), _ptr(workspace), workspace.numel(),
+                                       _stream(stream))
+    _check(rc, "kvd_paged_decode_launch")
+    return out
+
+
+def paged_append(k_new, v_new, k_pool, v_pool, ks_pool, vs_pool, block_table, seq_lens, layout: str = "bhtd",
+                 stream=None) -> None:
+    """Quantise-on-append of one token per (b, kv head) into a paged cache."""
+    import torch
+
+    B, Hkv, D = k_new.shape
+    if v_new.stride() != k_new.stride() or v_pool.stride() != k_pool.stride() or vs_pool.stride() != ks_pool.stride():
+        raise ValueError("K/V (and their scales, and the new rows) must share strides")
+    q_like = torch.empty((B, Hkv, D), dtype=torch.float32, device="meta")
+    desc = make_paged_desc(q_like, k_pool, ks_pool, q_like, block_table, seq_lens, layout)
+    rc = lib().kvd_paged_append_int8_launch(ctypes.byref(desc), _ptr(k_new), _ptr(v_new), k_new.stride(0),
+                                            k_new.stride(1), _ptr(k_pool), _ptr(v_pool), _ptr(ks_pool),
+                                            _ptr(vs_pool), _ptr(seq_lens), _stream(stream))
+    _check(rc, "kvd_paged_append_int8_launch")
 
 
 def device_status() -> int:

@@ -121,6 +121,62 @@ cudaError_t kvd_decode_launch_noalloc(const kvd_decode_desc* desc,
                                       const float* k_scale, const float* v_scale, float* out,
                                       cudaStream_t stream);
 
+/* ------------------------------------------------------------------------ */
+/* Paged cache (no reference counterpart: the reference's caches are dense   */
+/* [H][S][D] arrays, kv_cache/new_kvint8.cu:83-84)                            */
+/* ------------------------------------------------------------------------ */
+
+/* K and V codes and their scales live in pools of fixed-size blocks of
+ * `block_size` tokens. Token t of sequence b, kv head h is at
+ *   K_pool[blk * kv_stride_block + h * kv_stride_h + (t % block_size) * kv_stride_t + d]
+ *   k_scale_pool[blk * sc_stride_block + h * sc_stride_h + (t % block_size)]
+ * with blk = block_table[b * block_table_stride + t / block_size] (V alike).
+ * Both common pool layouts are strides of this form: [blocks][Hkv][bs][D]
+ * (kv_stride_t = D) and [blocks][bs][Hkv][D] (kv_stride_t = Hkv*D). A block id
+ * outside [0, num_blocks) is not read: its tokens count as score 0 with a zero
+ * value and the device status word records KVD_STATUS_BAD_BLOCK. The decode
+ * uses the tensor-core kernel when head_dim is 128, the group size is 1, 2, 4,
+ * 8 or 16, block_size is a power of two >= 8, pools and strides are 16-byte
+ * aligned and scale strides are multiples of 4 floats; other shapes run on
+ * the generic kernel (any block_size >= 1). */
+#define KVD_STATUS_BAD_BLOCK 4
+typedef struct kvd_paged_desc {
+    int32_t batch, num_q_heads, num_kv_heads, head_dim;
+    int32_t block_size;          /* tokens per block, >= 1 */
+    int32_t num_blocks;          /* blocks in each pool */
+    int32_t max_blocks_per_seq;  /* table entries per sequence; lengths are clamped to this x block_size */
+    uint32_t flags;              /* KVD_FLAG_* */
+    const int32_t* seq_lens;     /* device [B] current lengths (required) */
+    const int32_t* block_table;  /* device [B][block_table_stride] pool block ids */
+    int64_t block_table_stride;  /* >= max_blocks_per_seq */
+    int64_t kv_stride_block, kv_stride_h, kv_stride_t;  /* K and V pools (elements) */
+    int64_t sc_stride_block, sc_stride_h;               /* scale pools (floats); token stride 1 */
+    int64_t q_stride_b, q_stride_h;
+    int64_t o_stride_b, o_stride_h;
+    float softmax_scale;         /* <= 0 selects 1/sqrt(D) */
+} kvd_paged_desc;
+
+size_t kvd_paged_workspace_size(const kvd_paged_desc* desc);
+
+/* Decode over a paged cache; workspace rules as for kvd_decode_launch. */
+cudaError_t kvd_paged_decode_launch(const kvd_paged_desc* desc,
+                                    const float* Q, const int8_t* K_pool, const int8_t* V_pool,
+                                    const float* k_scale_pool, const float* v_scale_pool, float* out,
+                                    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Quantise-on-append into a paged cache: the rule and the seq_lens update of
+ * kvd_append_int8_launch; token seq_lens[b] goes to the block the table names
+ * for it. A sequence already holding max_blocks_per_seq*block_size tokens is
+ * left unchanged (KVD_STATUS_CACHE_FULL); an out-of-range block id writes
+ * nothing and leaves the length unchanged (KVD_STATUS_BAD_BLOCK). Reads the
+ * batch/head/block/stride fields of `desc`; q/o strides and flags are unused. */
+cudaError_t kvd_paged_append_int8_launch(const kvd_paged_desc* desc,
+                                         const float* k_new, const float* v_new,
+                                         int64_t new_stride_b, int64_t new_stride_h,
+                                         int8_t* K_pool, int8_t* V_pool,
+                                         float* k_scale_pool, float* v_scale_pool,
+                                         int32_t* seq_lens, cudaStream_t stream);
+
 /* Log-sum-exp combine of `num_parts` partial-record arrays, each [num_heads]
  * records of KVD_PARTIAL_STRIDE(head_dim) floats, part p starting at
  * parts + p*part_stride. Writes normalised rows out[h*out_stride + d], or
@@ -156,8 +212,8 @@ cudaError_t kvd_quantize_rows_launch(const float* x, int64_t rows, int dim, int6
                                      int8_t* codes, int64_t code_stride, float* scales,
                                      cudaStream_t stream);
 
-/* Device status word: kernels record bounded-wait timeouts and cache overflow
- * here instead of trapping. kvd_device_status synchronises the current device,
+/* Device status word: kernels record bounded-wait timeouts, cache overflow
+ * and bad block ids (KVD_STATUS_BAD_BLOCK, above) here instead of trapping. kvd_device_status synchronises the current device,
  * reads the word, clears it and returns it through *status. */
 #define KVD_STATUS_OK 0
 #define KVD_STATUS_WAIT_TIMEOUT 1
