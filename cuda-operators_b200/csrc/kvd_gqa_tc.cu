@@ -279,7 +279,7 @@ struct __align__(16) GMeta {
 // of tokens 4l..4l+3 with one 16-byte load per pool and stores them into the
 // slot. Table reads run two tiles ahead and scale loads one tile ahead, so
 // neither latency stalls the issue. Each ring slot is armed once with the
-// sum of the bytes its lanes copy. K runs at most one tile ahead of V here.
+// sum of the bytes its lanes copy. K runs one tile ahead of V here.
 // A block id outside the pool is not read: its scales are zeroed (score 0,
 // weight 0) and the status word records it.
 struct PTile {
@@ -352,31 +352,40 @@ __device__ __forceinline__ void gqa_producer_paged(const CUtensorMap* kmap, cons
     const bool small = rows < C::TOK;
     const uint32_t box = static_cast<uint32_t>(rows) * C::D;
     int64_t ik = 0, iv = 0;  // tiles issued on each ring
+    // K boxes of tile T (this lane's box): wait for the slot, arm it, issue.
+    auto issue_k = [&](const PTile& T, int blk) -> bool {
+        const int tok = j * rows;
+        const bool good = tok < T.n && blk >= 0 && blk < p.nblk;
+        const int sk = static_cast<int>(ik % NK);
+        if (ik >= NK && !mbar_wait(&bars[C::B_KEMPTY + sk], static_cast<uint32_t>(((ik / NK) - 1) & 1)))
+            return false;
+        const uint32_t bytes = __reduce_add_sync(0xffffffffu, (lane < 16 && good) ? box : 0u);
+        if (lane == 0) mbar_arrive_expect_tx(&bars[C::B_KFULL + sk], bytes);
+        __syncwarp();
+        if (lane < 16 && good)
+            tma_load_4d(smem + C::OFF_KR + sk * C::TILE_BYTES + tok * C::D, kmap, 0, (T.t0 + tok) & (bs - 1), T.I.hk,
+                        blk, &bars[C::B_KFULL + sk], pol);
+        ++ik;
+        return true;
+    };
     PTile T0 = ptile_first(p);
     PTile T1 = ptile_next(p, T0);
     int b0 = ptile_block(p, T0, rows, lane), b1 = ptile_block(p, T1, rows, lane);
     float4 kq0, vq0;
     if (small) ptile_scales(p, T0, b0, lane, kq0, vq0);
-    while (T0.it < p.n_items) {
+    // K runs one tile ahead of V: K(T0) now, then each step issues K(T1) before V(T0).
+    bool ok = T0.it >= p.n_items || issue_k(T0, b0);
+    while (ok && T0.it < p.n_items) {
         const PTile T2 = ptile_next(p, T1);
         const int b2 = ptile_block(p, T2, rows, lane);  // two tiles ahead
         float4 kq1, vq1;
         if (small) ptile_scales(p, T1, b1, lane, kq1, vq1);  // one tile ahead
+        if (T1.it < p.n_items && !issue_k(T1, b1)) break;
         const int tok = j * rows;
         const bool act = tok < T0.n;
         const bool good = act && b0 >= 0 && b0 < p.nblk;
         if (act && !good && lane < 16) record_status(KVD_STATUS_BAD_BLOCK);
         const int off = (T0.t0 + tok) & (bs - 1);
-        // ---- K slot
-        const int sk = static_cast<int>(ik % NK);
-        if (ik >= NK && !mbar_wait(&bars[C::B_KEMPTY + sk], static_cast<uint32_t>(((ik / NK) - 1) & 1))) break;
-        uint32_t bytes = __reduce_add_sync(0xffffffffu, (lane < 16 && good) ? box : 0u);
-        if (lane == 0) mbar_arrive_expect_tx(&bars[C::B_KFULL + sk], bytes);
-        __syncwarp();
-        if (lane < 16 && good)
-            tma_load_4d(smem + C::OFF_KR + sk * C::TILE_BYTES + tok * C::D, kmap, 0, off, T0.I.hk, b0,
-                        &bars[C::B_KFULL + sk], pol);
-        ++ik;
         // ---- V slot: V boxes, scales, metadata
         const int sv = static_cast<int>(iv % NV);
         if (iv >= NV && !mbar_wait(&bars[C::B_VEMPTY + sv], static_cast<uint32_t>(((iv / NV) - 1) & 1))) break;
@@ -394,7 +403,7 @@ __device__ __forceinline__ void gqa_producer_paged(const CUtensorMap* kmap, cons
         if (lane == 0)
             meta[sv] = GMeta{T0.it, T0.n, (T0.tt == 0 ? 1 : 0) | (T0.tt == T0.I.ntiles - 1 ? 2 : 0), 0};
         const uint32_t mine = !good ? 0u : small ? (lane < 16 ? box : 0u) : (lane < 16 ? box + seg : lane == 16 ? seg : 0u);
-        bytes = __reduce_add_sync(0xffffffffu, mine);
+        const uint32_t bytes = __reduce_add_sync(0xffffffffu, mine);
         __syncwarp();
         if (lane == 0) mbar_arrive_expect_tx(&bars[C::B_VFULL + sv], bytes);
         __syncwarp();
