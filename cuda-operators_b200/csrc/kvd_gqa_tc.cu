@@ -583,6 +583,7 @@ __device__ __forceinline__ float warp_max(float x) {
 // values and collecting the warpgroup result.
 template <int K, bool MAX>
 __device__ __forceinline__ void epi_reduce_post(float (&v)[K], float* red, uint64_t* bar, uint32_t use) {
+    static_assert(K <= 16, "one 16-float row per warp");
     const int wq = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
@@ -595,10 +596,12 @@ __device__ __forceinline__ void epi_reduce_post(float (&v)[K], float* red, uint6
             v[k] = x;
         }
     }
-    float* rb = red + (use & 1u) * 128;
+    float* row = red + (use & 1u) * 128 + wq * 16;  // this warp's row of the exchange buffer
     if (lane == 0) {
 #pragma unroll
-        for (int k = 0; k < K; ++k) rb[wq * 32 + k] = v[k];
+        for (int k = 0; k + 4 <= K; k += 4) *reinterpret_cast<float4*>(row + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
+#pragma unroll
+        for (int k = K & ~3; k < K; ++k) row[k] = v[k];
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(bar);
@@ -610,9 +613,17 @@ __device__ __forceinline__ bool epi_reduce_finish(float (&v)[K], float* red, uin
     const float* rb = red + (use & 1u) * 128;
     ++use;
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-        const float a = rb[k], b = rb[32 + k], c = rb[64 + k], d = rb[96 + k];
-        v[k] = MAX ? fmaxf(fmaxf(a, b), fmaxf(c, d)) : (a + b) + (c + d);
+    for (int w = 0; w < 4; ++w) {
+        float t[K];
+#pragma unroll
+        for (int k = 0; k + 4 <= K; k += 4) {
+            const float4 q = *reinterpret_cast<const float4*>(rb + w * 16 + k);
+            t[k] = q.x; t[k + 1] = q.y; t[k + 2] = q.z; t[k + 3] = q.w;
+        }
+#pragma unroll
+        for (int k = K & ~3; k < K; ++k) t[k] = rb[w * 16 + k];
+#pragma unroll
+        for (int k = 0; k < K; ++k) v[k] = w == 0 ? t[k] : (MAX ? fmaxf(v[k], t[k]) : v[k] + t[k]);
     }
     return ok;
 }
@@ -819,6 +830,7 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
 #pragma unroll
             for (int x = 0; x < CPW / 4; ++x) W[x] = 0u;
             int FB[HPW];
+            const int ea = 30 - exp_above(vsmax);
 #pragma unroll
             for (int h = 0; h < HPW; ++h) {
                 const float tmax = rv[h];  // same in every thread of the warpgroup
@@ -829,15 +841,13 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
                 const float pr = valid ? ex2_fast(sc[h] - m[h]) : 0.f;
                 l[h] += pr;
                 // Weight exponent: p <= 2^(tmax - m) <= 2^ceil(tmax - m) and v_scale < 2^exp_above(vsmax),
-                // so w * 2^F < 2^30 with F = 30 - ceil(tmax - m) - exp_above(vsmax).
-                int F = 0;
-                if (tmax != -INFINITY) {
-                    const float d = tmax - m[h];
-                    const int ep = d > -126.f ? static_cast<int>(ceilf(d)) : -126;
-                    F = min(126, max(-126, 30 - ep - exp_above(vsmax)));
-                }
+                // so w * 2^F < 2^30 with F = 30 - ceil(tmax - m) - exp_above(vsmax). A tile without
+                // valid tokens (tmax = -inf, NaN difference) gets ceil = -126 and weights 0.
+                const int ep = __float2int_ru(fmaxf(tmax - m[h], -126.f));
+                const int F = min(126, max(-126, ea - ep));
                 FB[h] = F;
-                W[h] = valid ? __float2uint_rn(pr * vsv * pow2i(F)) : 0u;
+                // pr = 0 and v_scale = 0 for invalid tokens, so W = 0 there without a select.
+                W[h] = __float2uint_rn(pr * (vsv * __int_as_float(F * 8388608 + 1065353216)));
             }
             uint8_t* wb = smem + C::OFF_WB + bi * C::WB_BYTES;
 #pragma unroll
