@@ -714,9 +714,11 @@ __device__ __forceinline__ bool gqa_pv_epi(const GqaParams& p, uint8_t* smem, ui
 #pragma unroll
     for (int h = 0; h < HPW; ++h) {
         const float f = combine_limbs(orr[4 * h], orr[4 * h + 1], orr[4 * h + 2], orr[4 * h + 3]);
-        const float al = (mpv[h] == mA[h]) ? 1.f : ex2_fast(mpv[h] - mA[h]);
-        o[h] = fmaf(f, pow2i(-FA[h]), o[h] * al);
-        mpv[h] = mA[h];
+        if (mpv[h] != mA[h]) {  // the running max moved (rare): rescale the accumulated output
+            o[h] *= ex2_fast(mpv[h] - mA[h]);
+            mpv[h] = mA[h];
+        }
+        o[h] = fmaf(f, __int_as_float(1065353216 - FA[h] * 8388608), o[h]);
     }
     if (A.flags & 2) {
         const GItem I = gqa_item(p, A.it);
