@@ -33,12 +33,22 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 thread_local int tl_launches = 0;
 
+// Known flags; one Q type, one output type, and typed output only for
+// normalised rows (records are fp32).
+bool flags_ok(uint32_t f) {
+    if ((f & ~(KVD_FLAG_PARTIAL_OUT | kDtypeFlags)) != 0) return false;
+    if ((f & KVD_FLAG_Q_BF16) && (f & KVD_FLAG_Q_F16)) return false;
+    if ((f & KVD_FLAG_OUT_BF16) && (f & KVD_FLAG_OUT_F16)) return false;
+    if ((f & KVD_FLAG_PARTIAL_OUT) && (f & (KVD_FLAG_OUT_BF16 | KVD_FLAG_OUT_F16))) return false;
+    return true;
+}
+
 cudaError_t check_desc(const kvd_decode_desc* d) {
     if (d == nullptr) return cudaErrorInvalidValue;
     if (d->batch < 1 || d->num_q_heads < 1 || d->num_kv_heads < 1 || d->head_dim < 1) return cudaErrorInvalidValue;
     if (d->num_q_heads % d->num_kv_heads != 0) return cudaErrorInvalidValue;
     if (d->max_seq_len < 0) return cudaErrorInvalidValue;
-    if ((d->flags & ~KVD_FLAG_PARTIAL_OUT) != 0) return cudaErrorInvalidValue;
+    if (!flags_ok(d->flags)) return cudaErrorInvalidValue;
     return cudaSuccess;
 }
 
@@ -47,7 +57,7 @@ size_t fast_prefix_bytes(const kvd_decode_desc& d) {
 }
 }  // namespace
 
-bool fast_path_ok(const kvd_decode_desc& d, const float* Q, const int8_t* K, const int8_t* V) {
+bool fast_path_ok(const kvd_decode_desc& d, const void* Q, const int8_t* K, const int8_t* V) {
     if (d.head_dim != 64 && d.head_dim != 128) return false;
     if (!aligned16(Q) || !aligned16(K) || !aligned16(V)) return false;
     if (((d.kv_stride_b | d.kv_stride_h) & 15) != 0) return false;
@@ -79,9 +89,9 @@ extern "C" size_t kvd_workspace_size(const kvd_decode_desc* desc) {
     return need > gqa ? need : gqa;
 }
 
-extern "C" cudaError_t kvd_decode_launch(const kvd_decode_desc* desc, const float* Q, const int8_t* K,
+extern "C" cudaError_t kvd_decode_launch(const kvd_decode_desc* desc, const void* Q, const int8_t* K,
                                          const int8_t* V, const float* k_scale, const float* v_scale,
-                                         float* out, void* workspace, size_t workspace_bytes,
+                                         void* out, void* workspace, size_t workspace_bytes,
                                          cudaStream_t stream) {
     tl_launches = 0;
     cudaError_t e = check_desc(desc);
@@ -100,8 +110,11 @@ extern "C" cudaError_t kvd_decode_launch(const kvd_decode_desc* desc, const floa
     // D=128 takes it too: the tensor cores do QK and PV, so the SMs spend far
     // fewer instructions (and watts) per byte than the CUDA-core kernel.
     const bool mha_tc = KVD_MHA_TENSOR_CORES >= 2 || (KVD_MHA_TENSOR_CORES == 1 && !d.seq_lens);
-    if ((d.num_q_heads > d.num_kv_heads || mha_tc) && gqa_path_ok(d))
+    if ((d.num_q_heads > d.num_kv_heads || mha_tc || (d.flags & kDtypeFlags)) && gqa_path_ok(d))
         return launch_gqa_tc(d, Q, K, V, k_scale, v_scale, out, workspace, workspace_bytes, stream, &tl_launches);
+    if (d.flags & kDtypeFlags)  // the CUDA-core split-KV kernel reads and writes fp32 only
+        return launch_generic(d, Q, K, V, k_scale, v_scale, out, workspace, workspace_bytes, stream,
+                              &tl_launches);
 
     const int tok = tile_tokens(d.head_dim);
     const size_t pre = fast_prefix_bytes(d);
@@ -110,7 +123,8 @@ extern "C" cudaError_t kvd_decode_launch(const kvd_decode_desc* desc, const floa
                               &tl_launches);
 
     DecodeParams p{};
-    p.Q = Q; p.K = K; p.V = V; p.ks = k_scale; p.vs = v_scale; p.out = out;
+    p.Q = static_cast<const float*>(Q); p.K = K; p.V = V; p.ks = k_scale; p.vs = v_scale;
+    p.out = static_cast<float*>(out);
     p.B = d.batch; p.Hq = d.num_q_heads; p.Hkv = d.num_kv_heads; p.D = d.head_dim;
     p.group = d.num_q_heads / d.num_kv_heads;
     p.S = d.max_seq_len;
@@ -160,7 +174,7 @@ cudaError_t check_paged(const kvd_paged_desc* d) {
     if (d->block_size < 1 || d->num_blocks < 1 || d->max_blocks_per_seq < 1) return cudaErrorInvalidValue;
     if (d->block_table_stride < d->max_blocks_per_seq) return cudaErrorInvalidValue;
     if (static_cast<int64_t>(d->max_blocks_per_seq) * d->block_size > 0x7fffffffLL) return cudaErrorInvalidValue;
-    if ((d->flags & ~KVD_FLAG_PARTIAL_OUT) != 0) return cudaErrorInvalidValue;
+    if (!flags_ok(d->flags)) return cudaErrorInvalidValue;
     return cudaSuccess;
 }
 
@@ -192,7 +206,7 @@ bool paged_tc_shape(const kvd_paged_desc& p, const kvd_decode_desc& d) {
     return bs >= 8 && (bs & (bs - 1)) == 0 && gqa_path_ok(d);
 }
 
-bool paged_tc_ok(const kvd_paged_desc& p, const kvd_decode_desc& d, const float* Q, const int8_t* K,
+bool paged_tc_ok(const kvd_paged_desc& p, const kvd_decode_desc& d, const void* Q, const int8_t* K,
                  const int8_t* V, const float* ks, const float* vs) {
     if (!paged_tc_shape(p, d)) return false;
     if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(ks) || !aligned16(vs)) return false;
@@ -213,9 +227,9 @@ extern "C" size_t kvd_paged_workspace_size(const kvd_paged_desc* desc) {
     return gen > gqa ? gen : gqa;
 }
 
-extern "C" cudaError_t kvd_paged_decode_launch(const kvd_paged_desc* desc, const float* Q, const int8_t* K_pool,
+extern "C" cudaError_t kvd_paged_decode_launch(const kvd_paged_desc* desc, const void* Q, const int8_t* K_pool,
                                                const int8_t* V_pool, const float* k_scale_pool,
-                                               const float* v_scale_pool, float* out, void* workspace,
+                                               const float* v_scale_pool, void* out, void* workspace,
                                                size_t workspace_bytes, cudaStream_t stream) {
     tl_launches = 0;
     cudaError_t e = check_paged(desc);
@@ -251,11 +265,11 @@ extern "C" cudaError_t kvd_paged_append_int8_launch(const kvd_paged_desc* desc, 
 }
 
 extern "C" cudaError_t kvd_combine_launch(const float* parts, int num_parts, int64_t part_stride, int num_heads,
-                                          int head_dim, float* out, int64_t out_stride, uint32_t flags,
+                                          int head_dim, void* out, int64_t out_stride, uint32_t flags,
                                           cudaStream_t stream) {
     tl_launches = 0;
     if (!parts || !out || num_parts < 1 || num_heads < 1 || head_dim < 1) return cudaErrorInvalidValue;
-    if ((flags & ~KVD_FLAG_PARTIAL_OUT) != 0) return cudaErrorInvalidValue;
+    if (!flags_ok(flags) || (flags & (KVD_FLAG_Q_BF16 | KVD_FLAG_Q_F16))) return cudaErrorInvalidValue;
     if (part_stride < static_cast<int64_t>(num_heads) * (head_dim + 4) && num_parts > 1) return cudaErrorInvalidValue;
     return launch_combine_parts(parts, num_parts, part_stride, num_heads, head_dim, out, out_stride, flags, stream,
                                 &tl_launches);

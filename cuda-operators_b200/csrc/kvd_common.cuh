@@ -5,6 +5,8 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "kvdecode.h"
@@ -29,6 +31,21 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 __device__ __forceinline__ void record_status(int32_t code) {
     atomicOr(&g_status, code);
+}
+
+// ------------------------------------------------- query / output element types
+// Query element `off` of Q, whose type KVD_FLAG_Q_* in `flags` selects.
+__device__ __forceinline__ float load_q(const void* Q, int64_t off, uint32_t flags) {
+    if (flags & KVD_FLAG_Q_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(Q)[off]);
+    if (flags & KVD_FLAG_Q_F16) return __half2float(static_cast<const __half*>(Q)[off]);
+    return static_cast<const float*>(Q)[off];
+}
+
+// Stores a normalised output element in the type KVD_FLAG_OUT_* selects.
+__device__ __forceinline__ void store_out(void* out, int64_t off, float v, uint32_t flags) {
+    if (flags & KVD_FLAG_OUT_BF16) static_cast<__nv_bfloat16*>(out)[off] = __float2bfloat16_rn(v);
+    else if (flags & KVD_FLAG_OUT_F16) static_cast<__half*>(out)[off] = __float2half_rn(v);
+    else static_cast<float*>(out)[off] = v;
 }
 
 // ---------------------------------------------------------------- mbarrier

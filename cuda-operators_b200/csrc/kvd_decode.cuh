@@ -53,6 +53,9 @@ struct DecodeParams {
 #define KVD_SK64_CTAS 2
 #endif
 
+// Element-type flags of Q and of the output rows.
+constexpr uint32_t kDtypeFlags = KVD_FLAG_Q_BF16 | KVD_FLAG_Q_F16 | KVD_FLAG_OUT_BF16 | KVD_FLAG_OUT_F16;
+
 // Route MHA with head_dim 128 to the tensor-core kernel: 1 = dense batches,
 // 2 = dense and ragged batches, 0 = never (CUDA-core split-KV kernel).
 #ifndef KVD_MHA_TENSOR_CORES
@@ -90,7 +93,7 @@ struct PagedView {
     int64_t kv_sblk, kv_st, sc_sblk;
 };
 
-bool fast_path_ok(const kvd_decode_desc& d, const float* Q, const int8_t* K, const int8_t* V);
+bool fast_path_ok(const kvd_decode_desc& d, const void* Q, const int8_t* K, const int8_t* V);
 
 // Per-device cached properties.
 int device_sm_count();
@@ -99,24 +102,24 @@ int device_sm_count();
 cudaError_t launch_plan(const int32_t* seq_lens, int B, int Hq, int tok, int cap, int32_t* prefix,
                         cudaStream_t st, int* launches);
 cudaError_t launch_splitkv(const DecodeParams& p, cudaStream_t st, int* launches);
-cudaError_t launch_generic(const kvd_decode_desc& d, const float* Q, const int8_t* K,
-                           const int8_t* V, const float* ks, const float* vs, float* out,
+cudaError_t launch_generic(const kvd_decode_desc& d, const void* Q, const int8_t* K,
+                           const int8_t* V, const float* ks, const float* vs, void* out,
                            void* ws, size_t ws_bytes, cudaStream_t st, int* launches,
                            const PagedView* pv = nullptr);
 size_t generic_workspace_size(const kvd_decode_desc& d);
 cudaError_t launch_combine_records(const float* base, int nparts, int64_t part_stride, int64_t rec_stride,
-                                   int64_t rows, int rows_per_b, int D, float* out, int64_t o_sb, int64_t o_sh,
+                                   int64_t rows, int rows_per_b, int D, void* out, int64_t o_sb, int64_t o_sh,
                                    uint32_t flags, cudaStream_t st, int* launches);
 bool gqa_path_ok(const kvd_decode_desc& d);
 size_t gqa_workspace_size(const kvd_decode_desc& d);
-cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const float* Q, const int8_t* K, const int8_t* V,
-                          const float* ks, const float* vs, float* out, void* ws, size_t ws_bytes,
+cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const void* Q, const int8_t* K, const int8_t* V,
+                          const float* ks, const float* vs, void* out, void* ws, size_t ws_bytes,
                           cudaStream_t st, int* launches, const PagedView* pv = nullptr);
 cudaError_t launch_paged_append(const kvd_paged_desc& d, const float* k_new, const float* v_new, int64_t new_sb,
                                 int64_t new_sh, int8_t* K, int8_t* V, float* ks, float* vs, int32_t* seq_lens,
                                 cudaStream_t st);
 cudaError_t launch_combine_parts(const float* parts, int num_parts, int64_t part_stride, int num_heads,
-                                 int head_dim, float* out, int64_t out_stride, uint32_t flags,
+                                 int head_dim, void* out, int64_t out_stride, uint32_t flags,
                                  cudaStream_t st, int* launches);
 
 }  // namespace kvd

@@ -17,12 +17,12 @@ constexpr int kGenMaxD = 512;
 constexpr int kGenDPT = kGenMaxD / kGenThreads;  // dims per thread
 
 struct GenParams {
-    const float* Q;
+    const void* Q;  // fp32, bf16 or fp16 (flags)
     const int8_t* K;
     const int8_t* V;
     const float* ks;
     const float* vs;
-    float* out;
+    void* out;        // normalised rows (fp32, bf16 or fp16) or fp32 records
     float* partials;  // [units][splits] records of D+4 floats, or nullptr when splits == 1
     const int32_t* seq_lens;
     int B, Hq, D, group, S, splits, span;
@@ -67,8 +67,8 @@ __global__ void __launch_bounds__(kGenThreads) generic_decode_kernel(const GenPa
     const int len = p.seq_lens ? min(max(0, p.seq_lens[b]), p.S) : p.S;  // clamp to the capacity
     const int t_lo = min(len, split * p.span), t_hi = min(len, (split + 1) * p.span);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const float* q = p.Q + b * p.q_sb + static_cast<int64_t>(hq) * p.q_sh;
-    for (int d = tid; d < p.D; d += kGenThreads) qs[d] = q[d] * p.qscale;
+    const int64_t q0 = b * p.q_sb + static_cast<int64_t>(hq) * p.q_sh;
+    for (int d = tid; d < p.D; d += kGenThreads) qs[d] = load_q(p.Q, q0 + d, p.flags) * p.qscale;
     float acc[kGenDPT];
 #pragma unroll
     for (int j = 0; j < kGenDPT; ++j) acc[j] = 0.f;
@@ -122,16 +122,16 @@ __global__ void __launch_bounds__(kGenThreads) generic_decode_kernel(const GenPa
     const bool partial_out = (p.flags & KVD_FLAG_PARTIAL_OUT) != 0;
     float* rec;
     if (p.splits == 1) {
-        float* row = p.out + b * p.o_sb + static_cast<int64_t>(hq) * p.o_sh;
+        const int64_t ro = b * p.o_sb + static_cast<int64_t>(hq) * p.o_sh;
         if (!partial_out) {
 #pragma unroll
             for (int j = 0; j < kGenDPT; ++j) {
                 const int d = tid + j * kGenThreads;
-                if (d < p.D) row[d] = l > 0.f ? acc[j] / l : 0.f;
+                if (d < p.D) store_out(p.out, ro + d, l > 0.f ? acc[j] / l : 0.f, p.flags);
             }
             return;
         }
-        rec = row;
+        rec = static_cast<float*>(p.out) + ro;
     } else {
         rec = p.partials + (u * p.splits + split) * static_cast<int64_t>(p.D + 4);
     }
@@ -147,13 +147,13 @@ __global__ void __launch_bounds__(kGenThreads) generic_decode_kernel(const GenPa
 // + r*rec_stride) into normalised output rows or combined records.
 __global__ void __launch_bounds__(128) combine_records_kernel(
     const float* base, int nparts, int64_t part_stride, int64_t rec_stride, int rows_per_b, int D,
-    float* out, int64_t o_sb, int64_t o_sh, uint32_t flags) {
+    void* out, int64_t o_sb, int64_t o_sh, uint32_t flags) {
     const int64_t r = blockIdx.x;
     const float* first = base + r * rec_stride;
     float M = -INFINITY;
     for (int k = 0; k < nparts; ++k) M = fmaxf(M, first[k * part_stride]);
     const int b = static_cast<int>(r / rows_per_b), h = static_cast<int>(r % rows_per_b);
-    float* row = out + b * o_sb + static_cast<int64_t>(h) * o_sh;
+    const int64_t ro = b * o_sb + static_cast<int64_t>(h) * o_sh;
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         float O = 0.f, L = 0.f;
         if (M != -INFINITY) {
@@ -165,10 +165,11 @@ __global__ void __launch_bounds__(128) combine_records_kernel(
             }
         }
         if (flags & KVD_FLAG_PARTIAL_OUT) {
+            float* row = static_cast<float*>(out) + ro;
             if (d == 0) { row[0] = M; row[1] = L; }
             row[4 + d] = O;
         } else {
-            row[d] = L > 0.f ? O / L : 0.f;
+            store_out(out, ro + d, L > 0.f ? O / L : 0.f, flags);
         }
     }
 }
@@ -190,8 +191,8 @@ size_t generic_workspace_size(const kvd_decode_desc& d) {
     return static_cast<size_t>(d.batch) * d.num_q_heads * splits * (d.head_dim + 4) * sizeof(float);
 }
 
-cudaError_t launch_generic(const kvd_decode_desc& d, const float* Q, const int8_t* K,
-                           const int8_t* V, const float* ks, const float* vs, float* out,
+cudaError_t launch_generic(const kvd_decode_desc& d, const void* Q, const int8_t* K,
+                           const int8_t* V, const float* ks, const float* vs, void* out,
                            void* ws, size_t ws_bytes, cudaStream_t st, int* launches, const PagedView* pv) {
     if (d.head_dim > kGenMaxD) return cudaErrorInvalidValue;
     const int64_t units = static_cast<int64_t>(d.batch) * d.num_q_heads;
@@ -237,7 +238,7 @@ cudaError_t launch_generic(const kvd_decode_desc& d, const float* Q, const int8_
 }
 
 cudaError_t launch_combine_records(const float* base, int nparts, int64_t part_stride, int64_t rec_stride,
-                                   int64_t rows, int rows_per_b, int D, float* out, int64_t o_sb, int64_t o_sh,
+                                   int64_t rows, int rows_per_b, int D, void* out, int64_t o_sb, int64_t o_sh,
                                    uint32_t flags, cudaStream_t st, int* launches) {
     combine_records_kernel<<<static_cast<unsigned>(rows), 128, 0, st>>>(base, nparts, part_stride, rec_stride,
                                                                          rows_per_b, D, out, o_sb, o_sh, flags);
@@ -249,7 +250,7 @@ cudaError_t launch_combine_records(const float* base, int nparts, int64_t part_s
 // Public combine for partials gathered from several GPUs: part k holds
 // num_heads records at parts + k*part_stride.
 cudaError_t launch_combine_parts(const float* parts, int num_parts, int64_t part_stride, int num_heads,
-                                 int head_dim, float* out, int64_t out_stride, uint32_t flags,
+                                 int head_dim, void* out, int64_t out_stride, uint32_t flags,
                                  cudaStream_t st, int* launches) {
     combine_records_kernel<<<num_heads, 128, 0, st>>>(parts, num_parts, part_stride, head_dim + 4,
                                                       num_heads, head_dim, out, 0, out_stride, flags);

@@ -40,10 +40,10 @@
 namespace kvd {
 
 struct GqaParams {
-    const float* Q;
+    const void* Q;                // fp32, bf16 or fp16 (flags)
     const float* ks;
     const float* vs;
-    float* out;
+    void* out;                 // normalised rows (fp32, bf16 or fp16) or fp32 records
     float* partials;           // [B*Hq][P] records of D+4 floats when P > 1
     const int32_t* seq_lens;   // device [B] or nullptr
     const int32_t* order;      // ragged: sequences sorted by length, longest first; else nullptr
@@ -651,11 +651,11 @@ __device__ __forceinline__ bool gqa_qlimbs(const GqaParams& p, uint8_t* smem, in
     float* red = reinterpret_cast<float*>(smem + C::OFF_RED) + wg * 256;
     const GItem I = gqa_item(p, it);
     const int h0 = wg * HPW;
-    const float* q = p.Q + I.b * p.q_sb + static_cast<int64_t>(I.hk * G + h0) * p.q_sh + r;
+    const int64_t q0 = I.b * p.q_sb + static_cast<int64_t>(I.hk * G + h0) * p.q_sh + r;
     float qv[HPW], am[HPW];
 #pragma unroll
     for (int h = 0; h < HPW; ++h) {
-        qv[h] = __ldg(q + h * p.q_sh) * p.qscale;
+        qv[h] = load_q(p.Q, q0 + h * p.q_sh, p.flags) * p.qscale;
         am[h] = fabsf(qv[h]);
     }
     if (!epi_reduce<HPW, true>(am, red, red_bar, use)) return false;
@@ -727,13 +727,13 @@ __device__ __forceinline__ bool gqa_pv_epi(const GqaParams& p, uint8_t* smem, ui
 #pragma unroll
         for (int h = 0; h < HPW; ++h) {
             const int hq = I.hk * G + wg * HPW + h;
-            float* row = p.out + I.b * p.o_sb + static_cast<int64_t>(hq) * p.o_sh;
+            const int64_t ro = I.b * p.o_sb + static_cast<int64_t>(hq) * p.o_sh;
             if (!records) {
-                row[r] = LA[h] > 0.f ? o[h] / LA[h] : 0.f;
+                store_out(p.out, ro + r, LA[h] > 0.f ? o[h] / LA[h] : 0.f, p.flags);
             } else {
                 float* rec = split_row
                     ? p.partials + ((static_cast<int64_t>(I.b) * p.Hq + hq) * p.P + I.split) * (C::D + 4)
-                    : row;
+                    : static_cast<float*>(p.out) + ro;
                 if (r == 0) { rec[0] = mA[h]; rec[1] = LA[h]; }
                 rec[4 + r] = o[h];
             }
@@ -979,7 +979,7 @@ __global__ void __launch_bounds__(1024) seq_order_kernel(const int32_t* seq_lens
 // Ragged batches: merge the split records of rows whose sequence had more
 // than one split (single-split rows were written by the decode kernel).
 __global__ void __launch_bounds__(128) gqa_ragged_combine_kernel(const float* partials, const int32_t* seq_lens,
-                                                                 int Hq, int P, int span, int S, int D, float* out,
+                                                                 int Hq, int P, int span, int S, int D, void* out,
                                                                  int64_t o_sb, int64_t o_sh, uint32_t flags) {
     const int64_t r = blockIdx.x;
     const int b = static_cast<int>(r / Hq), hq = static_cast<int>(r - static_cast<int64_t>(b) * Hq);
@@ -989,7 +989,7 @@ __global__ void __launch_bounds__(128) gqa_ragged_combine_kernel(const float* pa
     const float* first = partials + r * P * static_cast<int64_t>(D + 4);
     float M = -INFINITY;
     for (int k = 0; k < ns; ++k) M = fmaxf(M, first[k * (D + 4)]);
-    float* row = out + b * o_sb + static_cast<int64_t>(hq) * o_sh;
+    const int64_t ro = b * o_sb + static_cast<int64_t>(hq) * o_sh;
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         float O = 0.f, L = 0.f;
         if (M != -INFINITY) {
@@ -1001,10 +1001,11 @@ __global__ void __launch_bounds__(128) gqa_ragged_combine_kernel(const float* pa
             }
         }
         if (flags & KVD_FLAG_PARTIAL_OUT) {
+            float* row = static_cast<float*>(out) + ro;
             if (d == 0) { row[0] = M; row[1] = L; }
             row[4 + d] = O;
         } else {
-            row[d] = L > 0.f ? O / L : 0.f;
+            kvd::store_out(out, ro + d, L > 0.f ? O / L : 0.f, flags);
         }
     }
 }
@@ -1161,8 +1162,8 @@ size_t gqa_workspace_size(const kvd_decode_desc& d) {
     return g.order_bytes + g.rec_bytes;
 }
 
-cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const float* Q, const int8_t* K, const int8_t* V,
-                          const float* ks, const float* vs, float* out, void* ws, size_t ws_bytes,
+cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const void* Q, const int8_t* K, const int8_t* V,
+                          const float* ks, const float* vs, void* out, void* ws, size_t ws_bytes,
                           cudaStream_t st, int* launches, const PagedView* pv) {
     const int G = d.num_q_heads / d.num_kv_heads;
     const GqaPlan g = plan_gqa(d, ws ? ws_bytes : 0);

@@ -65,9 +65,9 @@ cudaError_t noalloc_scratch_address(void** out) {
 }  // namespace
 }  // namespace kvd
 
-extern "C" cudaError_t kvd_decode_launch_noalloc(const kvd_decode_desc* desc, const float* Q, const int8_t* K,
+extern "C" cudaError_t kvd_decode_launch_noalloc(const kvd_decode_desc* desc, const void* Q, const int8_t* K,
                                                  const int8_t* V, const float* k_scale, const float* v_scale,
-                                                 float* out, cudaStream_t stream) {
+                                                 void* out, cudaStream_t stream) {
     if (desc == nullptr || !Q || !K || !V || !k_scale || !v_scale || !out) return cudaErrorInvalidValue;
     const size_t need = kvd_workspace_size(desc);
     if (need > KVD_NOALLOC_SCRATCH_BYTES) {

@@ -24,6 +24,10 @@ LIB_PATH = HERE / "libkvdecode_b200.so"
 HEADER = ROOT / "include" / "kvdecode.h"
 
 KVD_FLAG_PARTIAL_OUT = 1
+KVD_FLAG_Q_BF16 = 2
+KVD_FLAG_Q_F16 = 4
+KVD_FLAG_OUT_BF16 = 8
+KVD_FLAG_OUT_F16 = 16
 KVD_STATUS_OK = 0
 KVD_STATUS_WAIT_TIMEOUT = 1
 KVD_STATUS_CACHE_FULL = 2
@@ -213,6 +217,27 @@ def kv_int8_simple_launch(Q, K_int8, V_int8, k_scale, v_scale, output, num_heads
 
 
 # ----------------------------------------------------------------- extended API
+def dtype_flags(q=None, out=None, partial: bool = False) -> int:
+    """Decode flags for the element types of ``q`` and ``out`` (torch tensors:
+    float32, bfloat16 or float16)."""
+    import torch
+
+    f = KVD_FLAG_PARTIAL_OUT if partial else 0
+    qmap = {torch.float32: 0, torch.bfloat16: KVD_FLAG_Q_BF16, torch.float16: KVD_FLAG_Q_F16}
+    omap = {torch.float32: 0, torch.bfloat16: KVD_FLAG_OUT_BF16, torch.float16: KVD_FLAG_OUT_F16}
+    if q is not None:
+        if q.dtype not in qmap:
+            raise ValueError(f"unsupported query dtype {q.dtype}")
+        f |= qmap[q.dtype]
+    if out is not None and out.device.type != "meta":
+        if out.dtype not in omap:
+            raise ValueError(f"unsupported output dtype {out.dtype}")
+        if partial and out.dtype != torch.float32:
+            raise ValueError("partial records are float32")
+        f |= omap[out.dtype]
+    return f
+
+
 def make_desc(q, k, ks, out, seq_lens=None, max_seq_len: int | None = None, softmax_scale: float = 0.0,
               partial: bool = False) -> DecodeDesc:
     """Descriptor for q [B,Hq,D], k/v [B,Hkv,cap,D] int8, ks/vs [B,Hkv,cap], out [B,Hq,D or D+4]."""
@@ -225,7 +250,7 @@ def make_desc(q, k, ks, out, seq_lens=None, max_seq_len: int | None = None, soft
     d = DecodeDesc()
     d.batch, d.num_q_heads, d.num_kv_heads, d.head_dim = B, Hq, Hkv, D
     d.max_seq_len = cap if max_seq_len is None else max_seq_len
-    d.flags = KVD_FLAG_PARTIAL_OUT if partial else 0
+    d.flags = dtype_flags(q, out, partial)
     d.seq_lens = _ptr(seq_lens)
     d.kv_stride_b, d.kv_stride_h = k.stride(0), k.stride(1)
     d.sc_stride_b, d.sc_stride_h = ks.stride(0), ks.stride(1)
@@ -240,13 +265,15 @@ def workspace_size(desc: DecodeDesc) -> int:
 
 
 def decode(q, k, v, ks, vs, out=None, seq_lens=None, softmax_scale: float = 0.0, partial: bool = False,
-           workspace=None, max_seq_len: int | None = None, stream=None):
-    """Split-KV INT8 decode attention; returns ``out`` ([B,Hq,D], or [B,Hq,D+4] records if partial)."""
+           workspace=None, max_seq_len: int | None = None, stream=None, out_dtype=None):
+    """Split-KV INT8 decode attention; returns ``out`` ([B,Hq,D], or [B,Hq,D+4] records if partial).
+    ``q`` may be float32, bfloat16 or float16; the output type is ``out``'s (or ``out_dtype``,
+    default float32)."""
     import torch
 
     B, Hq, D = q.shape
     if out is None:
-        out = torch.empty((B, Hq, D + 4 if partial else D), dtype=torch.float32, device=q.device)
+        out = torch.empty((B, Hq, D + 4 if partial else D), dtype=out_dtype or torch.float32, device=q.device)
     if v.stride() != k.stride() or vs.stride() != ks.stride():
         raise ValueError("K/V and k_scale/v_scale must share strides")
     desc = make_desc(q, k, ks, out, seq_lens, max_seq_len, softmax_scale, partial)
@@ -274,16 +301,16 @@ def decode_noalloc(q, k, v, ks, vs, out, seq_lens=None, softmax_scale: float = 0
     return out
 
 
-def combine(parts, out=None, partial: bool = False, stream=None):
+def combine(parts, out=None, partial: bool = False, stream=None, out_dtype=None):
     """LSE-combine records ``parts`` [P, H, D+4] into out [H, D] (or [H, D+4] records)."""
     import torch
 
     P, H, R = parts.shape
     D = R - 4
     if out is None:
-        out = torch.empty((H, R if partial else D), dtype=torch.float32, device=parts.device)
+        out = torch.empty((H, R if partial else D), dtype=out_dtype or torch.float32, device=parts.device)
     rc = lib().kvd_combine_launch(_ptr(parts), P, parts.stride(0), H, D, _ptr(out), out.stride(0),
-                                  KVD_FLAG_PARTIAL_OUT if partial else 0, _stream(stream))
+                                  dtype_flags(None, out, partial), _stream(stream))
     _check(rc, "kvd_combine_launch")
     return out
 
@@ -342,7 +369,7 @@ def make_paged_desc(q, k_pool, ks_pool, out, block_table, seq_lens, layout: str 
     d = PagedDesc()
     d.batch, d.num_q_heads, d.num_kv_heads, d.head_dim = B, Hq, Hkv, D
     d.block_size, d.num_blocks, d.max_blocks_per_seq = bs, NB, block_table.shape[1]
-    d.flags = KVD_FLAG_PARTIAL_OUT if partial else 0
+    d.flags = dtype_flags(q if q.device.type != "meta" else None, out, partial)
     d.seq_lens, d.block_table = _ptr(seq_lens), _ptr(block_table)
     d.block_table_stride = block_table.stride(0)
     d.kv_stride_block, d.kv_stride_h, d.kv_stride_t = s_blk, s_h, s_t
@@ -358,13 +385,13 @@ def paged_workspace_size(desc: PagedDesc) -> int:
 
 
 def paged_decode(q, k_pool, v_pool, ks_pool, vs_pool, block_table, seq_lens, out=None, layout: str = "bhtd",
-                 softmax_scale: float = 0.0, partial: bool = False, workspace=None, stream=None):
+                 softmax_scale: float = 0.0, partial: bool = False, workspace=None, stream=None, out_dtype=None):
     """INT8 decode attention over a paged cache; returns ``out`` [B,Hq,D] (or records)."""
     import torch
 
     B, Hq, D = q.shape
     if out is None:
-        out = torch.empty((B, Hq, D + 4 if partial else D), dtype=torch.float32, device=q.device)
+        out = torch.empty((B, Hq, D + 4 if partial else D), dtype=out_dtype or torch.float32, device=q.device)
     if v_pool.stride() != k_pool.stride() or vs_pool.stride() != ks_pool.stride():
         raise ValueError("K/V pools and their scale pools must share strides")
     desc = make_paged_desc(q, k_pool, ks_pool, out, block_table, seq_lens, layout, softmax_scale, partial)

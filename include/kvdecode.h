@@ -66,6 +66,13 @@ cudaError_t kv_int8_simple_launch(const float* Q, const int8_t* K_int8, const in
 
 /* Decode flags. */
 #define KVD_FLAG_PARTIAL_OUT 1u  /* write (m, l, o) records instead of normalised output */
+/* Element type of Q (default fp32; strides stay in elements). */
+#define KVD_FLAG_Q_BF16 2u
+#define KVD_FLAG_Q_F16 4u
+/* Element type of the normalised output rows (default fp32; rounded to
+ * nearest even). Not combinable with KVD_FLAG_PARTIAL_OUT: records are fp32. */
+#define KVD_FLAG_OUT_BF16 8u
+#define KVD_FLAG_OUT_F16 16u
 
 /* A partial record (KVD_FLAG_PARTIAL_OUT output and kvd_combine_launch input)
  * is KVD_PARTIAL_STRIDE(D) floats: [0] = m, a reference point in base-2
@@ -99,10 +106,11 @@ size_t kvd_workspace_size(const kvd_decode_desc* desc);
 
 /* Split-KV flash decode. `workspace` may be smaller than kvd_workspace_size
  * (fewer splits are used) or NULL with workspace_bytes == 0. Concurrent calls
- * need separate workspaces. */
+ * need separate workspaces. Q and out are fp32 unless desc->flags selects
+ * bf16 or fp16 (KVD_FLAG_Q_*, KVD_FLAG_OUT_*). */
 cudaError_t kvd_decode_launch(const kvd_decode_desc* desc,
-                              const float* Q, const int8_t* K, const int8_t* V,
-                              const float* k_scale, const float* v_scale, float* out,
+                              const void* Q, const int8_t* K, const int8_t* V,
+                              const float* k_scale, const float* v_scale, void* out,
                               void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /* No counterpart in the reference. The same decode as kvd_decode_launch for
@@ -117,8 +125,8 @@ cudaError_t kvd_decode_launch(const kvd_decode_desc* desc,
  * nothing. */
 #define KVD_NOALLOC_SCRATCH_BYTES (512u * 1024u)
 cudaError_t kvd_decode_launch_noalloc(const kvd_decode_desc* desc,
-                                      const float* Q, const int8_t* K, const int8_t* V,
-                                      const float* k_scale, const float* v_scale, float* out,
+                                      const void* Q, const int8_t* K, const int8_t* V,
+                                      const float* k_scale, const float* v_scale, void* out,
                                       cudaStream_t stream);
 
 /* ------------------------------------------------------------------------ */
@@ -160,8 +168,8 @@ size_t kvd_paged_workspace_size(const kvd_paged_desc* desc);
 
 /* Decode over a paged cache; workspace rules as for kvd_decode_launch. */
 cudaError_t kvd_paged_decode_launch(const kvd_paged_desc* desc,
-                                    const float* Q, const int8_t* K_pool, const int8_t* V_pool,
-                                    const float* k_scale_pool, const float* v_scale_pool, float* out,
+                                    const void* Q, const int8_t* K_pool, const int8_t* V_pool,
+                                    const float* k_scale_pool, const float* v_scale_pool, void* out,
                                     void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /* Quantise-on-append into a paged cache: the rule and the seq_lens update of
@@ -179,11 +187,12 @@ cudaError_t kvd_paged_append_int8_launch(const kvd_paged_desc* desc,
 
 /* Log-sum-exp combine of `num_parts` partial-record arrays, each [num_heads]
  * records of KVD_PARTIAL_STRIDE(head_dim) floats, part p starting at
- * parts + p*part_stride. Writes normalised rows out[h*out_stride + d], or
- * combined records when flags has KVD_FLAG_PARTIAL_OUT. Used after gathering
- * per-GPU partials of a sequence split across GPUs. */
+ * parts + p*part_stride. Writes normalised rows out[h*out_stride + d] (fp32,
+ * or bf16/fp16 with KVD_FLAG_OUT_*), or combined records when flags has
+ * KVD_FLAG_PARTIAL_OUT. Used after gathering per-GPU partials of a sequence
+ * split across GPUs. */
 cudaError_t kvd_combine_launch(const float* parts, int num_parts, int64_t part_stride,
-                               int num_heads, int head_dim, float* out, int64_t out_stride,
+                               int num_heads, int head_dim, void* out, int64_t out_stride,
                                uint32_t flags, cudaStream_t stream);
 
 /* Quantise-on-append: for every (b, h), quantise the new fp32 K and V rows
