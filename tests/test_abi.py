@@ -60,7 +60,8 @@ def _desc(**kw):
 
 
 @pytest.mark.parametrize("kw", [dict(batch=0), dict(num_q_heads=6, num_kv_heads=4), dict(head_dim=0),
-                                dict(max_seq_len=-1), dict(flags=8), dict(flags=1, o_stride_h=128)])
+                                dict(max_seq_len=-1), dict(flags=64), dict(flags=1 | 8),
+                                dict(flags=1, o_stride_h=128)])
 def test_decode_launch_rejects_bad_descriptors(kw):
     d = _desc(**kw)
     rc = kvd.lib().kvd_decode_launch(ctypes.byref(d), 256, 256, 256, 256, 256, 256, None, 0, None)

@@ -95,7 +95,7 @@ def test_paged_symbols_and_argument_checks():
     d.seq_lens = d.block_table = 16
     assert L.kvd_paged_workspace_size(ctypes.byref(d)) == 0
     d.block_table_stride = 32
-    d.flags = 8  # unknown flag
+    d.flags = 64  # unknown flag
     assert L.kvd_paged_workspace_size(ctypes.byref(d)) == 0
 
 
