@@ -302,7 +302,11 @@ def run_ours(args) -> None:
                              out=out, workspace=ws)
             return
         if cfg.append:
-            case.seq_lens.copy_(lens0)
+            case.seq_lens.copy_(lens0)  # every step appends at the same positions
+            if not args.separate_append:  # quantise-on-append inside the decode launch
+                kvd.append_decode(case.k_new, case.v_new, case.q, case.K, case.V, case.ks, case.vs, case.seq_lens,
+                                  out=out, workspace=ws)
+                return
             kvd.append(case.k_new, case.v_new, case.K, case.V, case.ks, case.vs, case.seq_lens)
         kvd.decode(case.q, case.K, case.V, case.ks, case.vs, out=out, seq_lens=case.seq_lens, workspace=ws)
 
@@ -311,7 +315,8 @@ def run_ours(args) -> None:
         splitter.local_decode(case.q, case.K, case.V, case.ks, case.vs, splitter.records)
         launches_per_step = kvd.last_launch_count() + 1
     else:
-        launches_per_step = kvd.last_launch_count() + (1 if cfg.append else 0)
+        separate = cfg.append and (args.separate_append or pool is not None)
+        launches_per_step = kvd.last_launch_count() + (1 if separate else 0)
     for _ in range(args.warmup):
         step()
 
@@ -401,7 +406,9 @@ def run_ours(args) -> None:
                      "traffic": committed_traffic(args.config),
                      "timed": ("decode step: tcgen05 kernel gqa_tc_kernel" if cfg.head_dim == 128
                                else "decode step: CUDA-core split-KV kernel + boundary combine")
-                              + (" + NCCL record all-gather + LSE combine" if seqsplit else "")},
+                              + (" + NCCL record all-gather + LSE combine" if seqsplit else "")
+                              + ((" with the append fused into it" if not (args.separate_append or pool is not None)
+                                  else " after the append kernel") if cfg.append else "")},
         "clocks": clk.summary(),
         "e2e": {"value": e2e_gbs, "unit": "GB/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": int(q_host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4),
@@ -432,6 +439,8 @@ def main() -> None:
     ap.add_argument("--cpu-heads", type=int, default=512, help="query heads in the CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every step directly instead of from a CUDA graph")
+    ap.add_argument("--separate-append", action="store_true",
+                    help="config 4: append kernel then decode (default: one fused append+decode launch)")
     ap.add_argument("--paged", type=int, default=0, metavar="BS",
                     help="decode through the paged-cache entry point with BS-token blocks (0: dense cache)")
     args = ap.parse_args()

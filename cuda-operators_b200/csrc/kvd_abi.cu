@@ -287,6 +287,41 @@ extern "C" cudaError_t kvd_append_int8_launch(const kvd_append_desc* desc, const
     return e;
 }
 
+extern "C" cudaError_t kvd_append_decode_launch(const kvd_decode_desc* desc, const float* k_new,
+                                                const float* v_new, int64_t new_stride_b, int64_t new_stride_h,
+                                                const void* Q, int8_t* K, int8_t* V, float* k_scale, float* v_scale,
+                                                void* out, void* workspace, size_t workspace_bytes,
+                                                cudaStream_t stream) {
+    tl_launches = 0;
+    cudaError_t e = check_desc(desc);
+    if (e != cudaSuccess) return e;
+    const kvd_decode_desc& d = *desc;
+    if (!d.seq_lens || !k_new || !v_new || !Q || !K || !V || !k_scale || !v_scale || !out) return cudaErrorInvalidValue;
+    if (d.max_seq_len < 1) return cudaErrorInvalidValue;
+    if ((d.flags & KVD_FLAG_PARTIAL_OUT) && d.num_q_heads > 1 && d.o_stride_h < d.head_dim + 4)
+        return cudaErrorInvalidValue;
+    if (!workspace) workspace_bytes = 0;
+    int32_t* lens = const_cast<int32_t*>(d.seq_lens);
+    const bool rows16 = ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15) == 0 &&
+                        ((new_stride_b | new_stride_h) & 3) == 0;  // one 16-byte load per lane
+    if (rows16 && fast_path_ok(d, Q, K, V) && gqa_fused_append_ok(d, workspace_bytes)) {
+        const AppendView av{k_new, v_new, new_stride_b, new_stride_h, lens};
+        return launch_gqa_tc(d, Q, K, V, k_scale, v_scale, out, workspace, workspace_bytes, stream, &tl_launches,
+                             nullptr, &av);
+    }
+    // Two launches: the append kernel, then the decode of the grown cache.
+    kvd_append_desc a{};
+    a.batch = d.batch; a.num_kv_heads = d.num_kv_heads; a.head_dim = d.head_dim; a.capacity = d.max_seq_len;
+    a.kv_stride_b = d.kv_stride_b; a.kv_stride_h = d.kv_stride_h;
+    a.sc_stride_b = d.sc_stride_b; a.sc_stride_h = d.sc_stride_h;
+    a.new_stride_b = new_stride_b; a.new_stride_h = new_stride_h;
+    e = launch_append(a, k_new, v_new, K, V, k_scale, v_scale, lens, stream);
+    if (e != cudaSuccess) return e;
+    e = kvd_decode_launch(desc, Q, K, V, k_scale, v_scale, out, workspace, workspace_bytes, stream);
+    tl_launches += 1;
+    return e;
+}
+
 extern "C" cudaError_t kvd_quantize_rows_launch(const float* x, int64_t rows, int dim, int64_t x_stride,
                                                 int8_t* codes, int64_t code_stride, float* scales,
                                                 cudaStream_t stream) {

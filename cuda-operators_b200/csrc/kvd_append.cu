@@ -12,30 +12,9 @@
 // the host function mirrors. This file must not be built with fast-math.
 #include "kvd_common.cuh"
 #include "kvd_decode.cuh"
+#include "kvd_quant.cuh"
 
 namespace kvd {
-
-// One warp quantises one row of `dim` floats.
-__device__ __forceinline__ void quantize_row_warp(const float* __restrict__ x, int dim,
-                                                  int8_t* __restrict__ codes, float* __restrict__ scale,
-                                                  int lane) {
-    float amax = 0.f;
-    for (int d = lane; d < dim; d += 32) amax = fmaxf(amax, fabsf(x[d]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if (amax == 0.f) {
-        for (int d = lane; d < dim; d += 32) codes[d] = 0;
-        if (lane == 0) *scale = 0.f;
-        return;
-    }
-    const float s = amax / 127.0f;
-    for (int d = lane; d < dim; d += 32) {
-        float r = rintf(x[d] / s);
-        r = fminf(fmaxf(r, -127.0f), 127.0f);
-        codes[d] = static_cast<int8_t>(r);
-    }
-    if (lane == 0) *scale = s;
-}
 
 // One block per sequence b: every (kv head, K|V) row of the new token is
 // quantised into slot seq_lens[b]; then the length is bumped once.

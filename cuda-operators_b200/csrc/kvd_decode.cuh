@@ -93,6 +93,15 @@ struct PagedView {
     int64_t kv_sblk, kv_st, sc_sblk;
 };
 
+// Fused quantise-on-append for launch_gqa_tc: the new token's fp32 K/V rows
+// and the lengths, which the launch reads as seq_lens[b] + 1 and then updates.
+struct AppendView {
+    const float* k_new;
+    const float* v_new;
+    int64_t new_sb, new_sh;
+    int32_t* seq_lens;
+};
+
 bool fast_path_ok(const kvd_decode_desc& d, const void* Q, const int8_t* K, const int8_t* V);
 
 // Per-device cached properties.
@@ -114,7 +123,9 @@ bool gqa_path_ok(const kvd_decode_desc& d);
 size_t gqa_workspace_size(const kvd_decode_desc& d);
 cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const void* Q, const int8_t* K, const int8_t* V,
                           const float* ks, const float* vs, void* out, void* ws, size_t ws_bytes,
-                          cudaStream_t st, int* launches, const PagedView* pv = nullptr);
+                          cudaStream_t st, int* launches, const PagedView* pv = nullptr,
+                          const AppendView* av = nullptr);
+bool gqa_fused_append_ok(const kvd_decode_desc& d, size_t ws_bytes);
 cudaError_t launch_paged_append(const kvd_paged_desc& d, const float* k_new, const float* v_new, int64_t new_sb,
                                 int64_t new_sh, int8_t* K, int8_t* V, float* ks, float* vs, int32_t* seq_lens,
                                 cudaStream_t st);

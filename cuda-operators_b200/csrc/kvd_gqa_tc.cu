@@ -36,6 +36,7 @@
 
 #include "kvd_common.cuh"
 #include "kvd_decode.cuh"
+#include "kvd_quant.cuh"
 
 namespace kvd {
 
@@ -56,6 +57,21 @@ struct GqaParams {
     const int32_t* table;
     int64_t bt_stride, sc_sblk;
     int lbs, nblk;
+    // Fused quantise-on-append (k_new != nullptr, dense cache): token
+    // seq_lens[b] of every (b, kv head) is quantised from k_new / v_new into
+    // the cache before the tile that holds it is loaded, every length reads as
+    // seq_lens[b] + 1 (clamped to S), and the last CTA to finish writes the new
+    // lengths back (done_ctas is zeroed by the order kernel).
+    const float* k_new;
+    const float* v_new;
+    int64_t new_sb, new_sh, kv_sb, kv_sh;
+    int8_t* Kw;
+    int8_t* Vw;
+    float* ksw;
+    float* vsw;
+    int32_t* lens_rw;
+    unsigned int* done_ctas;
+    int len_add;
 };
 
 template <int G, int NK_, int NV_>
@@ -84,13 +100,14 @@ struct GqaCfg {
     static constexpr int OFF_META = OFF_RED + NWG * 2 * 4 * 32 * 4;  // [NV] x 16 bytes
     static constexpr int OFF_BAR = OFF_META + NV * 16;
     // barriers: kfull[NK], kempty[NK], vfull[NV], vempty[NV], s_full[2], s_free[2], w_full[2],
-    // o_full[2], o_free[2], q_full[2], red[NWG], done, drain
+    // o_full[2], o_free[2], q_full[2], red[NWG], done, drain, append
     static constexpr int B_KFULL = 0, B_KEMPTY = NK, B_VFULL = 2 * NK, B_VEMPTY = 2 * NK + NV;
     static constexpr int B_SFULL = 2 * NK + 2 * NV, B_SFREE = B_SFULL + 2, B_WFULL = B_SFREE + 2,
                          B_OFULL = B_WFULL + 2, B_OFREE = B_OFULL + 2, B_QFULL = B_OFREE + 2, B_RED = B_QFULL + 2,
-                         B_DONE = B_RED + NWG, B_DRAIN = B_DONE + 1;
-    static constexpr int NBAR = B_DRAIN + 1;
-    static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
+                         B_DONE = B_RED + NWG, B_DRAIN = B_DONE + 1, B_APPEND = B_DRAIN + 1;
+    static constexpr int NBAR = B_APPEND + 1;
+    static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;  // TMEM address, then the fused-append list count
+    static constexpr int OFF_APPENDED = OFF_TMEM + 8;
     static constexpr int SMEM_USED = OFF_TMEM + 16;
     static constexpr int SMEM_BYTES = SMEM_USED + 1024;           // slack to align the base to 1024
     static_assert(G >= 1 && G <= 16 && G % NWG == 0 && CPW % 16 == 0, "group size");
@@ -235,7 +252,14 @@ struct GItem {
 // skipped by every role, except split 0 of an empty sequence, which still
 // writes its zero output.
 __device__ __forceinline__ int seq_len_of(const GqaParams& p, int b) {
-    return p.seq_lens ? min(max(0, __ldg(p.seq_lens + b)), p.S) : p.S;
+    return p.seq_lens ? min(max(0, __ldg(p.seq_lens + b)) + p.len_add, p.S) : p.S;
+}
+
+// Fused append: the cache position of sequence b's new token, or -1 when the
+// cache is full (no append).
+__device__ __forceinline__ int append_pos(const GqaParams& p, int b) {
+    const int len = max(0, __ldg(p.seq_lens + b));
+    return len < p.S ? len : -1;
 }
 
 __device__ __forceinline__ int split_count(const GqaParams& p, int len) {
@@ -446,12 +470,19 @@ __device__ __forceinline__ void gqa_producer(const CUtensorMap* kmap, const CUte
     uint32_t round_par = 0;
     bool wrapped = false, ok = true;
     int64_t issued = 0;
+    bool appended = p.k_new == nullptr;  // fused append finished (or none)
     for (int it = next_item(p, blockIdx.x); it < p.n_items && ok; it = next_item(p, it + p.grid)) {
         const GItem I = gqa_item(p, it);
+        const int apos = appended ? -1 : append_pos(p, I.b);
         for (int tt = 0; tt < I.ntiles; ++tt) {
             if (wrapped && !mbar_wait(&empty[s], round_par ^ 1u)) { ok = false; break; }
             const int t0 = I.t_lo + tt * C::TOK;
             const int n = max(0, min(C::TOK, I.t_hi - t0));
+            // the first tile holding a new token waits for the epilogue warps to have written them all
+            if (!appended && apos >= t0 && apos < t0 + n) {
+                if (!mbar_wait(&bars[C::B_APPEND], 0)) { ok = false; break; }
+                appended = true;
+            }
             if (!v_side) {
                 mbar_arrive_expect_tx(&full[s], n > 0 ? static_cast<uint32_t>(C::TILE_BYTES) : 0u);
                 if (n > 0) tma_load_4d(smem + C::OFF_KR + s * C::TILE_BYTES, kmap, 0, t0, I.hk, I.b, &full[s], pol);
@@ -680,6 +711,71 @@ __device__ __forceinline__ bool gqa_qlimbs(const GqaParams& p, uint8_t* smem, in
     return true;
 }
 
+// Fused append, done by the epilogue warps before their first tile: the
+// CTA's candidate items (blockIdx.x + j * grid) are tested in parallel, one
+// per epilogue thread, and those whose range holds sequence b's new token are
+// listed as (b * Hkv + kv head, position) in shared memory (the reduction
+// buffer, free at this point); each warp then quantises the K and V rows of
+// every EW-th listed item, four at a time with their loads in flight together
+// (one float4 per lane, the rule and bits of quantize_row_warp), makes the
+// writes visible to the TMA engine and arrives on the append barrier, which
+// the producer waits on before the first tile holding a new token.
+template <int G, int NK, int NV>
+__device__ __forceinline__ void fused_append_rows(const GqaParams& p, uint8_t* smem) {
+    using C = GqaCfg<G, NK, NV>;
+    constexpr int ET = 128 * C::NWG;  // epilogue threads
+    constexpr int EW = ET / 32;
+    const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+    int* count = reinterpret_cast<int*>(smem + C::OFF_APPENDED);
+    int* list = reinterpret_cast<int*>(smem + C::OFF_RED);  // NWG * 256 ints = 2 per epilogue thread
+    const int per_cta = (p.n_items - static_cast<int>(blockIdx.x) + p.grid - 1) / p.grid;
+    for (int base = 0; base < per_cta; base += ET) {
+        if (t == 0) *count = 0;
+        named_bar_sync(1, ET);
+        if (base + t < per_cta) {
+            const int it = static_cast<int>(blockIdx.x) + (base + t) * p.grid;
+            const GItem I = gqa_item(p, it);
+            const int apos = append_pos(p, I.b);
+            if (apos >= I.t_lo && apos < I.t_hi) {
+                const int e = atomicAdd(count, 1);
+                list[2 * e] = I.b * p.Hkv + I.hk;
+                list[2 * e + 1] = apos;
+            }
+        }
+        named_bar_sync(1, ET);
+        const int n = *count;
+        // up to four rows per round with all their loads in flight together
+        for (int e0 = w; e0 < n; e0 += 4 * EW) {
+            float4 xk[4], xv[4];
+            int64_t crow[4], srow[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int e = e0 + j * EW;
+                if (e < n) {
+                    const int bh = list[2 * e], apos = list[2 * e + 1];
+                    const int b = bh / p.Hkv, hk = bh - b * p.Hkv;
+                    const int64_t nrow = b * p.new_sb + hk * p.new_sh + 4 * lane;
+                    xk[j] = __ldg(reinterpret_cast<const float4*>(p.k_new + nrow));
+                    xv[j] = __ldg(reinterpret_cast<const float4*>(p.v_new + nrow));
+                    crow[j] = b * p.kv_sb + hk * p.kv_sh + static_cast<int64_t>(apos) * C::D;
+                    srow[j] = b * p.sc_sb + hk * p.sc_sh + apos;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (e0 + j * EW < n) {
+                    quantize_row128_regs(xk[j], p.Kw + crow[j], p.ksw + srow[j], lane);
+                    quantize_row128_regs(xv[j], p.Vw + crow[j], p.vsw + srow[j], lane);
+                }
+            }
+        }
+        named_bar_sync(1, ET);  // the list is rewritten by the next chunk
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(reinterpret_cast<uint64_t*>(smem + C::OFF_BAR) + C::B_APPEND);
+}
+
 struct PvSnap {
     int64_t i;
     int it, flags;
@@ -760,6 +856,8 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
     const GMeta* meta = reinterpret_cast<const GMeta*>(smem + C::OFF_META);
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16) + wg * CPW;
     uint32_t use = 0;
+
+    if (p.k_new) fused_append_rows<G, NK, NV>(p, smem);
 
     // Zero this warpgroup's rows of both query-limb buffers (pad rows stay
     // zero), then item 0's limbs (its reduction orders the zeroing first).
@@ -882,6 +980,27 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
     if (A.i >= 0) gqa_pv_epi<G, NK, NV>(p, smem, tmem, A, mA, FA, LA, o, mpv);
 }
 
+// Fused append, end of a CTA: once every thread of the CTA is past its last
+// length read, count the CTA; the last CTA of the grid writes the new lengths
+// (seq_lens[b] + 1, or KVD_STATUS_CACHE_FULL when the cache was full).
+__device__ __forceinline__ void fused_append_finish(const GqaParams& p) {
+    __shared__ int last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(p.done_ctas, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last) {
+        __threadfence();
+        for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
+            const int len = max(0, p.lens_rw[b]);
+            if (len < p.S) p.lens_rw[b] = len + 1;
+            else record_status(KVD_STATUS_CACHE_FULL);
+        }
+    }
+}
+
 template <int G, int NK, int NV, int MINB>
 __global__ void __launch_bounds__(GqaCfg<G, NK, NV>::THREADS, MINB) gqa_tc_kernel(
     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const GqaParams p) {
@@ -889,7 +1008,10 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV>::THREADS, MINB) gqa_tc_kerne
     constexpr int EW = 4 * C::NWG;  // epilogue warps; then the producer warp, then the MMA warp
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    if (next_item(p, blockIdx.x) >= p.n_items) return;  // no (non-empty) item for this CTA
+    if (next_item(p, blockIdx.x) >= p.n_items) {  // no (non-empty) item for this CTA
+        if (p.k_new) fused_append_finish(p);
+        return;
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     uint64_t* done = bars + C::B_DONE;
@@ -914,6 +1036,8 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV>::THREADS, MINB) gqa_tc_kerne
         for (int wg = 0; wg < C::NWG; ++wg) mbar_init(&bars[C::B_RED + wg], 4);
         mbar_init(done, EW);
         mbar_init(drain, 1);
+        *reinterpret_cast<int*>(smem + C::OFF_APPENDED) = 0;
+        mbar_init(&bars[C::B_APPEND], EW);  // every epilogue warp, after its share of the fused append
         fence_mbar_init();
     }
     if (warp == EW + 1) tmem_alloc(reinterpret_cast<uint32_t*>(smem + C::OFF_TMEM), C::TMEM_COLS);
@@ -923,9 +1047,7 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV>::THREADS, MINB) gqa_tc_kerne
     if (warp == EW) {
         if (p.table) gqa_producer_paged<G, NK, NV>(&kmap, &vmap, p, smem);
         else if (lane < 2) gqa_producer<G, NK, NV>(&kmap, &vmap, p, smem, lane == 1);
-        return;
-    }
-    if (warp == EW + 1) {
+    } else if (warp == EW + 1) {
         if (lane == 0) {
             gqa_mma<G, NK, NV>(p, smem, tmem);
             mma_commit(drain);  // arrives once every MMA issued above has completed
@@ -935,26 +1057,29 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV>::THREADS, MINB) gqa_tc_kerne
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
-        return;
+    } else {
+        gqa_epilogue<G, NK, NV>(p, smem, tmem);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(done);
     }
-    gqa_epilogue<G, NK, NV>(p, smem, tmem);
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(done);
+    if (p.k_new) fused_append_finish(p);
 }
 
 }  // namespace kvd
 
 // Ragged batches: sequences sorted by length, longest first (one block,
 // bitonic sort of (length, index) keys; B <= 4096).
-__global__ void __launch_bounds__(1024) seq_order_kernel(const int32_t* seq_lens, int B, int S, int32_t* order) {
+__global__ void __launch_bounds__(1024) seq_order_kernel(const int32_t* seq_lens, int B, int S, int32_t* order,
+                                                        int len_add, unsigned int* done_ctas) {
     __shared__ unsigned long long keys[4096];
+    if (threadIdx.x == 0 && done_ctas) *done_ctas = 0u;
     int n2 = 1;
     while (n2 < B) n2 <<= 1;
     for (int i = threadIdx.x; i < n2; i += blockDim.x) {
         unsigned long long k = ~0ull;
         if (i < B) {
-            const int len = min(max(0, seq_lens[i]), S);
+            const int len = min(max(0, seq_lens[i]) + len_add, S);
             k = (static_cast<unsigned long long>(0x7FFFFFFF - len) << 32) | static_cast<unsigned>(i);
         }
         keys[i] = k;
@@ -1132,7 +1257,8 @@ GqaPlan plan_gqa(const kvd_decode_desc& d, size_t ws_limit) {
     const int64_t units = static_cast<int64_t>(d.batch) * d.num_kv_heads;
     const int64_t grid = static_cast<int64_t>(device_sm_count()) * kGqaCtas;
     const int s_tiles = (S + 127) / 128;
-    g.order_bytes = (d.seq_lens && d.batch <= 4096) ? ((static_cast<size_t>(d.batch) * 4 + 255) & ~size_t(255)) : 0;
+    // order array + one counter word (fused append)
+    g.order_bytes = (d.seq_lens && d.batch <= 4096) ? ((static_cast<size_t>(d.batch) * 4 + 4 + 255) & ~size_t(255)) : 0;
     int span_tiles;
     if (d.seq_lens) {
         // Ragged: split long sequences into items of at most 16 tiles (fewer if
@@ -1157,6 +1283,10 @@ GqaPlan plan_gqa(const kvd_decode_desc& d, size_t ws_limit) {
 }
 }  // namespace
 
+bool gqa_fused_append_ok(const kvd_decode_desc& d, size_t ws_bytes) {
+    return gqa_path_ok(d) && d.seq_lens && plan_gqa(d, ws_bytes).order_bytes > 0;
+}
+
 size_t gqa_workspace_size(const kvd_decode_desc& d) {
     const GqaPlan g = plan_gqa(d, ~size_t(0));
     return g.order_bytes + g.rec_bytes;
@@ -1164,10 +1294,11 @@ size_t gqa_workspace_size(const kvd_decode_desc& d) {
 
 cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const void* Q, const int8_t* K, const int8_t* V,
                           const float* ks, const float* vs, void* out, void* ws, size_t ws_bytes,
-                          cudaStream_t st, int* launches, const PagedView* pv) {
+                          cudaStream_t st, int* launches, const PagedView* pv, const AppendView* av) {
     const int G = d.num_q_heads / d.num_kv_heads;
     const GqaPlan g = plan_gqa(d, ws ? ws_bytes : 0);
     const int S = d.max_seq_len;
+    if (av && (pv || !g.order_bytes || !d.seq_lens)) return cudaErrorNotSupported;
     CUtensorMap km, vm;
     if (pv) {
         if (!make_paged_map(&km, K, d.num_kv_heads, *pv, d.kv_stride_h) ||
@@ -1201,9 +1332,22 @@ cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const void* Q, const int8_t*
     const float scale = d.softmax_scale > 0.f ? d.softmax_scale : 1.0f / sqrtf(static_cast<float>(d.head_dim));
     p.qscale = scale * 1.4426950408889634f;
     p.flags = d.flags;
+    unsigned int* done_ctas = nullptr;
+    if (av) {
+        p.k_new = av->k_new; p.v_new = av->v_new; p.new_sb = av->new_sb; p.new_sh = av->new_sh;
+        p.kv_sh = d.kv_stride_h > 0 ? d.kv_stride_h : static_cast<int64_t>(S) * 128;
+        p.kv_sb = d.kv_stride_b > 0 ? d.kv_stride_b : p.kv_sh * d.num_kv_heads;
+        p.Kw = const_cast<int8_t*>(K); p.Vw = const_cast<int8_t*>(V);
+        p.ksw = const_cast<float*>(ks); p.vsw = const_cast<float*>(vs);
+        p.lens_rw = av->seq_lens;
+        done_ctas = reinterpret_cast<unsigned int*>(static_cast<char*>(ws) + static_cast<size_t>(d.batch) * 4);
+        p.done_ctas = done_ctas;
+        p.len_add = 1;
+    }
     cudaError_t e;
     if (p.order) {
-        seq_order_kernel<<<1, 1024, 0, st>>>(d.seq_lens, d.batch, S, static_cast<int32_t*>(ws));
+        seq_order_kernel<<<1, 1024, 0, st>>>(d.seq_lens, d.batch, S, static_cast<int32_t*>(ws), p.len_add,
+                                             done_ctas);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         ++*launches;

@@ -125,6 +125,8 @@ _SIGNATURES = {
     "kvd_abi_version": (c_int, []),
     "kvd_error_string": (ctypes.c_char_p, [c_int]),
     "kvd_decode_launch_noalloc": (c_int, [ctypes.POINTER(DecodeDesc)] + [c_void_p] * 6 + [c_void_p]),
+    "kvd_append_decode_launch": (c_int, [ctypes.POINTER(DecodeDesc), c_void_p, c_void_p, c_int64, c_int64]
+                                 + [c_void_p] * 6 + [c_void_p, c_size_t, c_void_p]),
     "kvd_paged_workspace_size": (c_size_t, [ctypes.POINTER(PagedDesc)]),
     "kvd_paged_decode_launch": (c_int, [ctypes.POINTER(PagedDesc)] + [c_void_p] * 7 + [c_size_t, c_void_p]),
     "kvd_paged_append_int8_launch": (c_int, [ctypes.POINTER(PagedDesc), c_void_p, c_void_p, c_int64, c_int64]
@@ -328,6 +330,27 @@ def append(k_new, v_new, K, V, ks, vs, seq_lens, stream=None) -> None:
     rc = lib().kvd_append_int8_launch(ctypes.byref(d), _ptr(k_new), _ptr(v_new), _ptr(K), _ptr(V), _ptr(ks),
                                       _ptr(vs), _ptr(seq_lens), _stream(stream))
     _check(rc, "kvd_append_int8_launch")
+
+
+def append_decode(k_new, v_new, q, k, v, ks, vs, seq_lens, out=None, workspace=None, softmax_scale: float = 0.0,
+                  partial: bool = False, stream=None, out_dtype=None):
+    """Quantise-on-append of one token per (b, kv head) and the decode over the grown
+    cache in one decode launch (``kvd_append_decode_launch``); ``seq_lens`` is updated."""
+    import torch
+
+    B, Hq, D = q.shape
+    if out is None:
+        out = torch.empty((B, Hq, D + 4 if partial else D), dtype=out_dtype or torch.float32, device=q.device)
+    if v.stride() != k.stride() or vs.stride() != ks.stride() or v_new.stride() != k_new.stride():
+        raise ValueError("K/V (and their scales, and the new rows) must share strides")
+    desc = make_desc(q, k, ks, out, seq_lens, None, softmax_scale, partial)
+    if workspace is None:
+        workspace = torch.empty(max(workspace_size(desc), 1), dtype=torch.uint8, device=q.device)
+    rc = lib().kvd_append_decode_launch(ctypes.byref(desc), _ptr(k_new), _ptr(v_new), k_new.stride(0),
+                                        k_new.stride(1), _ptr(q), _ptr(k), _ptr(v), _ptr(ks), _ptr(vs), _ptr(out),
+                                        _ptr(workspace), workspace.numel(), _stream(stream))
+    _check(rc, "kvd_append_decode_launch")
+    return out
 
 
 def quantize_rows(x, codes=None, scales=None, stream=None):

@@ -214,6 +214,23 @@ cudaError_t kvd_append_int8_launch(const kvd_append_desc* desc,
                                    int8_t* K, int8_t* V, float* k_scale, float* v_scale,
                                    int32_t* seq_lens, cudaStream_t stream);
 
+/* No counterpart in the reference. kvd_append_int8_launch followed by
+ * kvd_decode_launch in one decode launch: the new token of every (b, kv head)
+ * (k_new/v_new + b*new_stride_b + h*new_stride_h, D floats each) is quantised
+ * with the same rule into position desc->seq_lens[b] of the cache, the decode
+ * attends over seq_lens[b] + 1 tokens including it, and seq_lens is then
+ * incremented (a sequence already at max_seq_len is left unchanged and
+ * records KVD_STATUS_CACHE_FULL). desc->seq_lens is required and is written.
+ * Results, cache contents and lengths are identical to the two separate calls.
+ * The fusion runs on the tensor-core kernel (head_dim 128, groups 1/2/4/8/16,
+ * B <= 4096, a workspace of at least kvd_workspace_size(desc)); other shapes
+ * run the two steps as two launches. */
+cudaError_t kvd_append_decode_launch(const kvd_decode_desc* desc,
+                                     const float* k_new, const float* v_new,
+                                     int64_t new_stride_b, int64_t new_stride_h,
+                                     const void* Q, int8_t* K, int8_t* V, float* k_scale, float* v_scale,
+                                     void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* Quantise `rows` contiguous fp32 rows of `dim` values (row stride x_stride
  * floats) to codes (row stride code_stride bytes) and one scale per row, with
  * the same rule as kvd_append_int8_launch. */
