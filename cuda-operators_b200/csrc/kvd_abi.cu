@@ -57,6 +57,8 @@ size_t fast_prefix_bytes(const kvd_decode_desc& d) {
 }
 }  // namespace
 
+int* launch_counter() { return &tl_launches; }
+
 bool fast_path_ok(const kvd_decode_desc& d, const void* Q, const int8_t* K, const int8_t* V) {
     if (d.head_dim != 64 && d.head_dim != 128) return false;
     if (!aligned16(Q) || !aligned16(K) || !aligned16(V)) return false;

@@ -104,6 +104,9 @@ struct AppendView {
 
 bool fast_path_ok(const kvd_decode_desc& d, const void* Q, const int8_t* K, const int8_t* V);
 
+// Launch count of the current host thread's last entry-point call (kvd_last_launch_count).
+int* launch_counter();
+
 // Per-device cached properties.
 int device_sm_count();
 

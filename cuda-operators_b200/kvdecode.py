@@ -127,6 +127,12 @@ _SIGNATURES = {
     "kvd_decode_launch_noalloc": (c_int, [ctypes.POINTER(DecodeDesc)] + [c_void_p] * 6 + [c_void_p]),
     "kvd_append_decode_launch": (c_int, [ctypes.POINTER(DecodeDesc), c_void_p, c_void_p, c_int64, c_int64]
                                  + [c_void_p] * 6 + [c_void_p, c_size_t, c_void_p]),
+    "kvd_mgpu_get_unique_id": (c_int, [c_void_p]),
+    "kvd_mgpu_comm_init": (c_int, [ctypes.POINTER(c_void_p), c_int, c_int, c_void_p]),
+    "kvd_mgpu_comm_destroy": (c_int, [c_void_p]),
+    "kvd_mgpu_seq_split_workspace_size": (c_size_t, [ctypes.POINTER(DecodeDesc), c_int]),
+    "kvd_mgpu_seq_split_decode": (c_int, [ctypes.POINTER(DecodeDesc)] + [c_void_p] * 6
+                                  + [c_void_p, c_size_t, c_void_p, c_int, c_void_p]),
     "kvd_paged_workspace_size": (c_size_t, [ctypes.POINTER(PagedDesc)]),
     "kvd_paged_decode_launch": (c_int, [ctypes.POINTER(PagedDesc)] + [c_void_p] * 7 + [c_size_t, c_void_p]),
     "kvd_paged_append_int8_launch": (c_int, [ctypes.POINTER(PagedDesc), c_void_p, c_void_p, c_int64, c_int64]
@@ -441,6 +447,53 @@ def paged_append(k_new, v_new, k_pool, v_pool, ks_pool, vs_pool, block_table, se
                                             k_new.stride(1), _ptr(k_pool), _ptr(v_pool), _ptr(ks_pool),
                                             _ptr(vs_pool), _ptr(seq_lens), _stream(stream))
     _check(rc, "kvd_paged_append_int8_launch")
+
+
+# ------------------------------------------------------------------ multi-GPU
+def mgpu_unique_id() -> bytes:
+    """A fresh 128-byte NCCL unique id (made on one rank, broadcast by the caller)."""
+    buf = (ctypes.c_ubyte * 128)()
+    rc = lib().kvd_mgpu_get_unique_id(ctypes.addressof(buf))
+    if rc != 0:
+        raise RuntimeError(f"kvd_mgpu_get_unique_id failed: nccl error {rc}")
+    return bytes(buf)
+
+
+class MgpuComm:
+    """An NCCL communicator made by the library (kvd_mgpu_comm_init)."""
+
+    def __init__(self, nranks: int, rank: int, uid: bytes):
+        buf = (ctypes.c_ubyte * 128).from_buffer_copy(uid)
+        h = c_void_p()
+        rc = lib().kvd_mgpu_comm_init(ctypes.byref(h), nranks, rank, ctypes.addressof(buf))
+        if rc != 0:
+            raise RuntimeError(f"kvd_mgpu_comm_init failed: nccl error {rc}")
+        self.handle, self.nranks, self.rank = h.value, nranks, rank
+
+    def close(self) -> None:
+        if self.handle:
+            lib().kvd_mgpu_comm_destroy(self.handle)
+            self.handle = None
+
+
+def seq_split_decode(comm: MgpuComm, q, k, v, ks, vs, out=None, seq_lens=None, workspace=None, stream=None,
+                     out_dtype=None):
+    """Sequence-split decode (kvd_mgpu_seq_split_decode): this rank passes its own token
+    range of the cache; every rank gets the merged output rows."""
+    import torch
+
+    B, Hq, D = q.shape
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=out_dtype or torch.float32, device=q.device)
+    desc = make_desc(q, k, ks, out, seq_lens)
+    if workspace is None:
+        n = int(lib().kvd_mgpu_seq_split_workspace_size(ctypes.byref(desc), comm.nranks))
+        workspace = torch.empty(max(n, 1), dtype=torch.uint8, device=q.device)
+    rc = lib().kvd_mgpu_seq_split_decode(ctypes.byref(desc), _ptr(q), _ptr(k), _ptr(v), _ptr(ks), _ptr(vs),
+                                         _ptr(out), _ptr(workspace), workspace.numel(), comm.handle, comm.nranks,
+                                         _stream(stream))
+    _check(rc, "kvd_mgpu_seq_split_decode")
+    return out
 
 
 def device_status() -> int:

@@ -238,6 +238,35 @@ cudaError_t kvd_quantize_rows_launch(const float* x, int64_t rows, int dim, int6
                                      int8_t* codes, int64_t code_stride, float* scales,
                                      cudaStream_t stream);
 
+/* ------------------------------------------------------------------------ */
+/* Multi-GPU sequence split (no reference counterpart: the reference is      */
+/* single-GPU). One process or host thread per GPU.                           */
+/* ------------------------------------------------------------------------ */
+
+/* NCCL communicator helpers. NCCL is loaded at run time (the copy already in
+ * the process if there is one, else libnccl.so.2); a caller may also pass a
+ * communicator of its own (an ncclComm_t) to the decode below. The id is the
+ * 128-byte ncclUniqueId; rank 0 makes it and the caller broadcasts it. Return
+ * values are ncclResult_t codes (0 = success). */
+int kvd_mgpu_get_unique_id(unsigned char* id /* [128] */);
+int kvd_mgpu_comm_init(void** comm, int nranks, int rank, const unsigned char* id /* [128] */);
+int kvd_mgpu_comm_destroy(void* comm);
+
+/* Sequence split over NCCL: this rank's K/V/scales hold its own token range of
+ * every sequence (a cache whose capacity is the range length; desc->seq_lens
+ * counts this rank's tokens, or NULL for max_seq_len each). The rank decodes
+ * its range into partial records, all-gathers the records of all `nranks`
+ * ranks over `comm` and merges them into normalised rows `out` (the same on
+ * every rank; typed per KVD_FLAG_OUT_*). Every rank must call it with the same
+ * batch, heads and head_dim, in the same order. NCCL errors return
+ * cudaErrorUnknown; a missing NCCL returns cudaErrorSharedObjectInitFailed. */
+size_t kvd_mgpu_seq_split_workspace_size(const kvd_decode_desc* desc, int nranks);
+cudaError_t kvd_mgpu_seq_split_decode(const kvd_decode_desc* desc,
+                                      const void* Q, const int8_t* K, const int8_t* V,
+                                      const float* k_scale, const float* v_scale, void* out,
+                                      void* workspace, size_t workspace_bytes,
+                                      void* comm, int nranks, cudaStream_t stream);
+
 /* Device status word: kernels record bounded-wait timeouts, cache overflow
  * and bad block ids (KVD_STATUS_BAD_BLOCK, above) here instead of trapping. kvd_device_status synchronises the current device,
  * reads the word, clears it and returns it through *status. */

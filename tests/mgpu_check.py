@@ -50,6 +50,30 @@ def main() -> int:
                 torch.cuda.synchronize()
                 b, err, _ = po.check(out.cpu().numpy(), ref[b0:b1])
                 bad += b
+        # the C-ABI path: a communicator made by the library, the id broadcast by torch
+        uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(kvd.mgpu_unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        comm = kvd.MgpuComm(world, rank, bytes(uid.cpu().numpy().tobytes()))
+        try:
+            for (B, Hq, Hkv, S, odt) in [(2, 8, 8, 4096, torch.float32), (3, 16, 2, 2500, torch.bfloat16)]:
+                q, K, V, ks, vs = po.random_cache(23 + Hq, B, Hq, Hkv, S, 128)
+                ref = po.decode_f64(q, K, V, ks, vs)
+                lo, hi = mg.seq_shard(S, world, rank, align=128)
+                shard = [torch.from_numpy(np.ascontiguousarray(a[:, :, lo:hi])).to(dev) for a in (K, V, ks, vs)]
+                for _ in range(2):
+                    out = kvd.seq_split_decode(comm, torch.from_numpy(q).to(dev), *shard, out_dtype=odt)
+                    torch.cuda.synchronize()
+                    o = out.float().cpu().numpy()
+                    tol = 2e-5 + (1e-4 + (2.0 ** -8 if odt == torch.bfloat16 else 0.0)) * np.abs(ref)
+                    b = int((np.abs(o - ref) > tol).sum()) + int((~np.isfinite(o)).sum())
+                    bad += b
+                    print(f"[rank {rank}] C-ABI seq split B={B} Hq={Hq} Hkv={Hkv} S={S} out={odt} "
+                          f"max_abs={np.abs(o - ref).max():.3g} bad={b} launches={kvd.last_launch_count()}",
+                          flush=True)
+        finally:
+            comm.close()
         flag = torch.tensor([bad], device=dev)
         dist.all_reduce(flag)
         bad = int(flag.item())
