@@ -260,6 +260,7 @@ def run_ours(args) -> None:
     # over NCCL (strong scaling: the job is one configuration-3 step). The other
     # configurations shard the batch with no communication (weak scaling).
     seqsplit = cfg.name == "long_context" and world > 1
+    comm = exchange = None
     if seqsplit:
         import dataclasses
 
@@ -271,6 +272,14 @@ def run_ours(args) -> None:
         job_bytes = wl.step_bytes(cfg, batch=B)
         nbytes = kvd.algorithmic_bytes(B, cfg.q_heads, cfg.kv_heads, cfg.head_dim, hi - lo)
         splitter = mg.SeqSplitDecode(B, cfg.q_heads, cfg.head_dim, dev)
+        if args.exchange != "torch":  # a communicator made by the library, its id broadcast by torch
+            uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+            if rank == 0:
+                uid.copy_(torch.frombuffer(bytearray(kvd.mgpu_unique_id()), dtype=torch.uint8))
+            dist.broadcast(uid, 0)
+            comm = kvd.MgpuComm(world, rank, bytes(uid.cpu().numpy().tobytes()))
+            if args.exchange == "p2p":
+                exchange = kvd.P2PExchange(comm, B, cfg.q_heads, cfg.head_dim)
     else:
         case = wl.make_case(cfg, seed=args.seed + rank, device=str(dev), batch=B)
     out = torch.empty((B, cfg.q_heads, cfg.head_dim), dtype=torch.float32, device=dev)
@@ -288,10 +297,18 @@ def run_ours(args) -> None:
         desc = kvd.make_desc(case.q, case.K, case.ks, out, case.seq_lens)
         ws = torch.empty(max(kvd.workspace_size(desc), 1), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
+    if seqsplit and args.exchange == "nccl":
+        ws_split = torch.empty(int(kvd.lib().kvd_mgpu_seq_split_workspace_size(__import__("ctypes").byref(desc),
+                                                                            world)), dtype=torch.uint8, device=dev)
 
     def step():  # launches on the current stream (a capture stream while a graph is recorded)
         if seqsplit:
-            splitter(case.q, case.K, case.V, case.ks, case.vs, out=out)
+            if args.exchange == "p2p":
+                exchange.decode(case.q, case.K, case.V, case.ks, case.vs, out=out)
+            elif args.exchange == "nccl":
+                kvd.seq_split_decode(comm, case.q, case.K, case.V, case.ks, case.vs, out=out, workspace=ws_split)
+            else:
+                splitter(case.q, case.K, case.V, case.ks, case.vs, out=out)
             return
         if pool is not None:
             if cfg.append:
@@ -311,9 +328,11 @@ def run_ours(args) -> None:
         kvd.decode(case.q, case.K, case.V, case.ks, case.vs, out=out, seq_lens=case.seq_lens, workspace=ws)
 
     step()
-    if seqsplit:  # this rank's partial decode, then the record combine
+    if seqsplit and args.exchange == "torch":  # this rank's partial decode, then the record combine
         splitter.local_decode(case.q, case.K, case.V, case.ks, case.vs, splitter.records)
         launches_per_step = kvd.last_launch_count() + 1
+    elif seqsplit:  # the library call counts its own launches (decode + exchange/combine)
+        launches_per_step = kvd.last_launch_count()
     else:
         separate = cfg.append and (args.separate_append or pool is not None)
         launches_per_step = kvd.last_launch_count() + (1 if separate else 0)
@@ -396,7 +415,9 @@ def run_ours(args) -> None:
                          f"D={cfg.head_dim} S={cfg.seq_len}" + (" ragged+append" if cfg.ragged else "")
                          + (f" paged cache, {args.paged}-token blocks in random pool order" if pool else "")),
             "global_batch": B if seqsplit else B * world, "seq_len": cfg.seq_len,
-            "parallelism": (f"sequence split x{world}, NCCL all-gather of (m, l, o) records + LSE combine"
+            "parallelism": (f"sequence split x{world}, (m, l, o) records exchanged "
+                            + ("by peer stores + LSE combine in one kernel" if args.exchange == "p2p"
+                               else "by NCCL all-gather + LSE combine")
                             if seqsplit else f"batch shards x{world}, no comm"),
             "bytes_per_step_per_gpu": nbytes,
             "l2": f"no flush: {nbytes / 1e9:.2f} GB of cache read per step > 126 MB L2",
@@ -406,7 +427,9 @@ def run_ours(args) -> None:
                      "traffic": committed_traffic(args.config),
                      "timed": ("decode step: tcgen05 kernel gqa_tc_kernel" if cfg.head_dim == 128
                                else "decode step: CUDA-core split-KV kernel + boundary combine")
-                              + (" + NCCL record all-gather + LSE combine" if seqsplit else "")
+                              + ((" + record exchange over NVLink peer stores and LSE combine in one kernel"
+                                  if args.exchange == "p2p" else " + NCCL record all-gather + LSE combine")
+                                 if seqsplit else "")
                               + ((" with the append fused into it" if not (args.separate_append or pool is not None)
                                   else " after the append kernel") if cfg.append else "")},
         "clocks": clk.summary(),
@@ -423,7 +446,12 @@ def run_ours(args) -> None:
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        dist.barrier()
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank unmaps its exchange buffers while a peer could still write them
+        if exchange is not None:
+            exchange.close()
+        if comm is not None:
+            comm.close()
         dist.destroy_process_group()
 
 
@@ -439,6 +467,9 @@ def main() -> None:
     ap.add_argument("--cpu-heads", type=int, default=512, help="query heads in the CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every step directly instead of from a CUDA graph")
+    ap.add_argument("--exchange", choices=["p2p", "nccl", "torch"], default="p2p",
+                    help="config 3 on N>1 GPUs: record exchange by peer stores (p2p), the library's NCCL call, "
+                         "or torch.distributed all_gather")
     ap.add_argument("--separate-append", action="store_true",
                     help="config 4: append kernel then decode (default: one fused append+decode launch)")
     ap.add_argument("--paged", type=int, default=0, metavar="BS",

@@ -133,6 +133,11 @@ _SIGNATURES = {
     "kvd_mgpu_seq_split_workspace_size": (c_size_t, [ctypes.POINTER(DecodeDesc), c_int]),
     "kvd_mgpu_seq_split_decode": (c_int, [ctypes.POINTER(DecodeDesc)] + [c_void_p] * 6
                                   + [c_void_p, c_size_t, c_void_p, c_int, c_void_p]),
+    "kvd_mgpu_p2p_create": (c_int, [ctypes.POINTER(c_void_p), c_int, c_int, c_int, c_void_p, c_int, c_int]),
+    "kvd_mgpu_p2p_destroy": (c_int, [c_void_p]),
+    "kvd_mgpu_p2p_workspace_size": (c_size_t, [ctypes.POINTER(DecodeDesc)]),
+    "kvd_mgpu_p2p_seq_split_decode": (c_int, [c_void_p, ctypes.POINTER(DecodeDesc)] + [c_void_p] * 6
+                                      + [c_void_p, c_size_t, c_void_p]),
     "kvd_paged_workspace_size": (c_size_t, [ctypes.POINTER(PagedDesc)]),
     "kvd_paged_decode_launch": (c_int, [ctypes.POINTER(PagedDesc)] + [c_void_p] * 7 + [c_size_t, c_void_p]),
     "kvd_paged_append_int8_launch": (c_int, [ctypes.POINTER(PagedDesc), c_void_p, c_void_p, c_int64, c_int64]
@@ -494,6 +499,38 @@ def seq_split_decode(comm: MgpuComm, q, k, v, ks, vs, out=None, seq_lens=None, w
                                          _stream(stream))
     _check(rc, "kvd_mgpu_seq_split_decode")
     return out
+
+
+class P2PExchange:
+    """Sequence-split exchange over NVLink peer stores (kvd_mgpu_p2p_*); collective to create."""
+
+    def __init__(self, comm: MgpuComm, batch: int, num_q_heads: int, head_dim: int):
+        h = c_void_p()
+        _check(lib().kvd_mgpu_p2p_create(ctypes.byref(h), batch, num_q_heads, head_dim, comm.handle, comm.nranks,
+                                         comm.rank), "kvd_mgpu_p2p_create")
+        self.handle = h.value
+        self._ws = None
+
+    def decode(self, q, k, v, ks, vs, out=None, seq_lens=None, stream=None, out_dtype=None):
+        import torch
+
+        B, Hq, D = q.shape
+        if out is None:
+            out = torch.empty((B, Hq, D), dtype=out_dtype or torch.float32, device=q.device)
+        desc = make_desc(q, k, ks, out, seq_lens)
+        n = int(lib().kvd_mgpu_p2p_workspace_size(ctypes.byref(desc)))
+        if self._ws is None or self._ws.numel() < n:
+            self._ws = torch.empty(max(n, 1), dtype=torch.uint8, device=q.device)
+        rc = lib().kvd_mgpu_p2p_seq_split_decode(self.handle, ctypes.byref(desc), _ptr(q), _ptr(k), _ptr(v),
+                                                 _ptr(ks), _ptr(vs), _ptr(out), _ptr(self._ws), self._ws.numel(),
+                                                 _stream(stream))
+        _check(rc, "kvd_mgpu_p2p_seq_split_decode")
+        return out
+
+    def close(self) -> None:
+        if self.handle:
+            lib().kvd_mgpu_p2p_destroy(self.handle)
+            self.handle = None
 
 
 def device_status() -> int:

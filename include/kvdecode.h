@@ -267,6 +267,26 @@ cudaError_t kvd_mgpu_seq_split_decode(const kvd_decode_desc* desc,
                                       void* workspace, size_t workspace_bytes,
                                       void* comm, int nranks, cudaStream_t stream);
 
+/* The same sequence split with the record exchange done by the library's own
+ * kernel over NVLink instead of NCCL: after the local decode, one kernel
+ * stores this rank's records straight into every rank's gather buffer (CUDA
+ * IPC mappings of peer memory), raises a flag per (rank, row block) in each
+ * peer's memory, waits for all ranks' flags of its rows (bounded: a rank that
+ * never arrives turns into KVD_STATUS_WAIT_TIMEOUT after 2 s) and merges them.
+ * kvd_mgpu_p2p_create is collective (every rank calls it with the same sizes):
+ * it allocates the exchange buffers (cudaMalloc) and swaps IPC handles once
+ * over `comm`. Up to 8 ranks, head_dim a multiple of 4. Every rank must make
+ * the same sequence of decode calls. */
+typedef struct kvd_mgpu_p2p kvd_mgpu_p2p;
+cudaError_t kvd_mgpu_p2p_create(kvd_mgpu_p2p** ctx, int batch, int num_q_heads, int head_dim,
+                                void* comm, int nranks, int rank);
+cudaError_t kvd_mgpu_p2p_destroy(kvd_mgpu_p2p* ctx);
+size_t kvd_mgpu_p2p_workspace_size(const kvd_decode_desc* desc);
+cudaError_t kvd_mgpu_p2p_seq_split_decode(kvd_mgpu_p2p* ctx, const kvd_decode_desc* desc,
+                                          const void* Q, const int8_t* K, const int8_t* V,
+                                          const float* k_scale, const float* v_scale, void* out,
+                                          void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* Device status word: kernels record bounded-wait timeouts, cache overflow
  * and bad block ids (KVD_STATUS_BAD_BLOCK, above) here instead of trapping. kvd_device_status synchronises the current device,
  * reads the word, clears it and returns it through *status. */

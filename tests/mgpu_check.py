@@ -72,6 +72,31 @@ def main() -> int:
                     print(f"[rank {rank}] C-ABI seq split B={B} Hq={Hq} Hkv={Hkv} S={S} out={odt} "
                           f"max_abs={np.abs(o - ref).max():.3g} bad={b} launches={kvd.last_launch_count()}",
                           flush=True)
+            # the peer-store exchange: one kernel pushes records over NVLink and merges
+            for (B, Hq, Hkv, S, odt) in [(2, 8, 8, 4096, torch.float32), (3, 16, 2, 2500, torch.float16)]:
+                q, K, V, ks, vs = po.random_cache(29 + Hq, B, Hq, Hkv, S, 128)
+                ref = po.decode_f64(q, K, V, ks, vs)
+                lo, hi = mg.seq_shard(S, world, rank, align=128)
+                shard = [torch.from_numpy(np.ascontiguousarray(a[:, :, lo:hi])).to(dev) for a in (K, V, ks, vs)]
+                ex = kvd.P2PExchange(comm, B, Hq, 128)
+                try:
+                    for step in range(5):  # several epochs: both buffer parities, flags counting up
+                        out = ex.decode(torch.from_numpy(q).to(dev), *shard, out_dtype=odt)
+                        torch.cuda.synchronize()
+                        o = out.float().cpu().numpy()
+                        extra = 2.0 ** -11 if odt == torch.float16 else 0.0
+                        tol = 2e-5 + 2.0 ** -24 + (1e-4 + extra) * np.abs(ref)
+                        b = int((np.abs(o - ref) > tol).sum()) + int((~np.isfinite(o)).sum())
+                        bad += b
+                        if step in (0, 4):
+                            print(f"[rank {rank}] P2P seq split B={B} Hq={Hq} S={S} out={odt} step={step} "
+                                  f"max_abs={np.abs(o - ref).max():.3g} bad={b} launches={kvd.last_launch_count()}",
+                                  flush=True)
+                    st = kvd.device_status()
+                    bad += int(st != 0)
+                finally:
+                    dist.barrier()  # no rank unmaps its buffers while a peer could still write them
+                    ex.close()
         finally:
             comm.close()
         flag = torch.tensor([bad], device=dev)
