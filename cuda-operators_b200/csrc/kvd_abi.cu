@@ -324,6 +324,34 @@ extern "C" cudaError_t kvd_append_decode_launch(const kvd_decode_desc* desc, con
     return e;
 }
 
+namespace {
+cudaError_t check_prefill(const kvd_prefill_desc* d) {
+    if (!d) return cudaErrorInvalidValue;
+    if (d->batch < 1 || d->num_q_heads < 1 || d->num_kv_heads < 1 || d->head_dim < 1) return cudaErrorInvalidValue;
+    if (d->num_q_heads % d->num_kv_heads != 0 || d->max_seq_len < 1 || d->max_queries < 1)
+        return cudaErrorInvalidValue;
+    if (!flags_ok(d->flags) || (d->flags & KVD_FLAG_PARTIAL_OUT)) return cudaErrorInvalidValue;
+    return cudaSuccess;
+}
+}  // namespace
+
+extern "C" size_t kvd_prefill_workspace_size(const kvd_prefill_desc* desc) {
+    (void)desc;
+    return 0;
+}
+
+extern "C" cudaError_t kvd_prefill_launch(const kvd_prefill_desc* desc, const void* Q, const int8_t* K,
+                                          const int8_t* V, const float* k_scale, const float* v_scale, void* out,
+                                          void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    tl_launches = 0;
+    cudaError_t e = check_prefill(desc);
+    if (e != cudaSuccess) return e;
+    if (!Q || !K || !V || !k_scale || !v_scale || !out) return cudaErrorInvalidValue;
+    (void)workspace;
+    (void)workspace_bytes;
+    return launch_generic_prefill(*desc, Q, K, V, k_scale, v_scale, out, stream, &tl_launches);
+}
+
 extern "C" cudaError_t kvd_quantize_rows_launch(const float* x, int64_t rows, int dim, int64_t x_stride,
                                                 int8_t* codes, int64_t code_stride, float* scales,
                                                 cudaStream_t stream) {

@@ -129,6 +129,8 @@ cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const void* Q, const int8_t*
                           cudaStream_t st, int* launches, const PagedView* pv = nullptr,
                           const AppendView* av = nullptr);
 bool gqa_fused_append_ok(const kvd_decode_desc& d, size_t ws_bytes);
+cudaError_t launch_generic_prefill(const kvd_prefill_desc& d, const void* Q, const int8_t* K, const int8_t* V,
+                                   const float* ks, const float* vs, void* out, cudaStream_t st, int* launches);
 cudaError_t launch_paged_append(const kvd_paged_desc& d, const float* k_new, const float* v_new, int64_t new_sb,
                                 int64_t new_sh, int8_t* K, int8_t* V, float* ks, float* vs, int32_t* seq_lens,
                                 cudaStream_t st);

@@ -30,6 +30,11 @@ struct GenParams {
     float qscale;
     uint32_t flags;
     PagedView pv;  // pv.table == nullptr: dense cache
+    // Causal prefill (Lq > 0): unit = (b, hq, query i); the queries are the last
+    // q_lens[b] cached tokens and query i attends to tokens [0, its position].
+    int Lq;
+    const int32_t* q_lens;
+    int64_t q_st, o_st;
 };
 
 // Code row offset and scale offset of token t of (b, kv head hk). A paged
@@ -58,16 +63,28 @@ __global__ void __launch_bounds__(kGenThreads) generic_decode_kernel(const GenPa
     __shared__ float qs[kGenMaxD];
     __shared__ float sc[kGenChunk];
     __shared__ float wt[kGenChunk];
+    __shared__ float pb[kGenChunk];
     __shared__ int64_t rowoff[kGenChunk];
     __shared__ float kscl[kGenChunk], vscl[kGenChunk];
     const int64_t u = blockIdx.x;
     const int split = blockIdx.y;
-    const int b = static_cast<int>(u / p.Hq), hq = static_cast<int>(u % p.Hq);
+    const int64_t bh = p.Lq > 0 ? u / p.Lq : u;
+    const int qi = p.Lq > 0 ? static_cast<int>(u - bh * p.Lq) : 0;
+    const int b = static_cast<int>(bh / p.Hq), hq = static_cast<int>(bh % p.Hq);
     const int hk = hq / p.group;
-    const int len = p.seq_lens ? min(max(0, p.seq_lens[b]), p.S) : p.S;  // clamp to the capacity
-    const int t_lo = min(len, split * p.span), t_hi = min(len, (split + 1) * p.span);
+    int len = p.seq_lens ? min(max(0, p.seq_lens[b]), p.S) : p.S;  // clamp to the capacity
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t q0 = b * p.q_sb + static_cast<int64_t>(hq) * p.q_sh;
+    if (p.Lq > 0) {  // prefill: this query's causal prefix
+        const int ql = p.q_lens ? min(max(0, p.q_lens[b]), p.Lq) : p.Lq;
+        const int64_t ro = b * p.o_sb + static_cast<int64_t>(hq) * p.o_sh + qi * p.o_st;
+        if (qi >= ql) {  // no such query: zero row
+            for (int d = tid; d < p.D; d += kGenThreads) store_out(p.out, ro + d, 0.f, p.flags);
+            return;
+        }
+        len = max(0, min(len, len - ql + qi + 1));
+    }
+    const int t_lo = min(len, split * p.span), t_hi = min(len, (split + 1) * p.span);
+    const int64_t q0 = b * p.q_sb + static_cast<int64_t>(hq) * p.q_sh + qi * p.q_st;
     for (int d = tid; d < p.D; d += kGenThreads) qs[d] = load_q(p.Q, q0 + d, p.flags) * p.qscale;
     float acc[kGenDPT];
 #pragma unroll
@@ -97,14 +114,14 @@ __global__ void __launch_bounds__(kGenThreads) generic_decode_kernel(const GenPa
         for (int t = 0; t < n; ++t) cm = fmaxf(cm, sc[t]);
         const float m_new = fmaxf(m, cm);
         const float alpha = exp2f(m - m_new);  // m == -inf -> 0
-        if (tid < n) {
+        if (tid < n) {  // into separate arrays: other threads may still be reading sc[] for the max
             const float pr = exp2f(sc[tid] - m_new);
-            sc[tid] = pr;
+            pb[tid] = pr;
             wt[tid] = pr * vscl[tid];
         }
         __syncthreads();
         float ps = 0.f;
-        for (int t = 0; t < n; ++t) ps += sc[t];
+        for (int t = 0; t < n; ++t) ps += pb[t];
         l = l * alpha + ps;
 #pragma unroll
         for (int j = 0; j < kGenDPT; ++j) {
@@ -122,7 +139,7 @@ __global__ void __launch_bounds__(kGenThreads) generic_decode_kernel(const GenPa
     const bool partial_out = (p.flags & KVD_FLAG_PARTIAL_OUT) != 0;
     float* rec;
     if (p.splits == 1) {
-        const int64_t ro = b * p.o_sb + static_cast<int64_t>(hq) * p.o_sh;
+        const int64_t ro = b * p.o_sb + static_cast<int64_t>(hq) * p.o_sh + qi * p.o_st;
         if (!partial_out) {
 #pragma unroll
             for (int j = 0; j < kGenDPT; ++j) {
@@ -204,7 +221,7 @@ cudaError_t launch_generic(const kvd_decode_desc& d, const void* Q, const int8_t
         if (fit < splits) splits = static_cast<int>(fit);
     }
     const int max_len = d.max_seq_len > 0 ? d.max_seq_len : 1;
-    GenParams p;
+    GenParams p{};
     p.Q = Q; p.K = K; p.V = V; p.ks = ks; p.vs = vs; p.out = out;
     p.partials = splits > 1 ? static_cast<float*>(ws) : nullptr;
     p.seq_lens = d.seq_lens;
@@ -235,6 +252,35 @@ cudaError_t launch_generic(const kvd_decode_desc& d, const void* Q, const int8_t
         ++*launches;
     }
     return cudaSuccess;
+}
+
+cudaError_t launch_generic_prefill(const kvd_prefill_desc& d, const void* Q, const int8_t* K, const int8_t* V,
+                                   const float* ks, const float* vs, void* out, cudaStream_t st, int* launches) {
+    if (d.head_dim > kGenMaxD) return cudaErrorInvalidValue;
+    GenParams p{};
+    p.Q = Q; p.K = K; p.V = V; p.ks = ks; p.vs = vs; p.out = out;
+    p.partials = nullptr;
+    p.seq_lens = d.seq_lens;
+    p.B = d.batch; p.Hq = d.num_q_heads; p.D = d.head_dim;
+    p.group = d.num_q_heads / d.num_kv_heads;
+    p.S = d.max_seq_len;
+    p.splits = 1;
+    p.span = d.max_seq_len > 0 ? d.max_seq_len : 1;
+    p.kv_sb = d.kv_stride_b; p.kv_sh = d.kv_stride_h;
+    p.sc_sb = d.sc_stride_b; p.sc_sh = d.sc_stride_h;
+    p.q_sb = d.q_stride_b; p.q_sh = d.q_stride_h;
+    p.o_sb = d.o_stride_b; p.o_sh = d.o_stride_h;
+    const float scale = d.softmax_scale > 0.f ? d.softmax_scale : 1.0f / sqrtf(static_cast<float>(d.head_dim));
+    p.qscale = scale * 1.4426950408889634f;
+    p.flags = d.flags;
+    p.pv = PagedView{};
+    p.Lq = d.max_queries; p.q_lens = d.q_lens; p.q_st = d.q_stride_t; p.o_st = d.o_stride_t;
+    const int64_t units = static_cast<int64_t>(d.batch) * d.num_q_heads * d.max_queries;
+    if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
+    generic_decode_kernel<<<dim3(static_cast<unsigned>(units), 1), kGenThreads, 0, st>>>(p);
+    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) ++*launches;
+    return e;
 }
 
 cudaError_t launch_combine_records(const float* base, int nparts, int64_t part_stride, int64_t rec_stride,

@@ -111,6 +111,33 @@ class PagedDesc(ctypes.Structure):
     ]
 
 
+class PrefillDesc(ctypes.Structure):
+    """Mirror of ``kvd_prefill_desc``."""
+
+    _fields_ = [
+        ("batch", c_int32),
+        ("num_q_heads", c_int32),
+        ("num_kv_heads", c_int32),
+        ("head_dim", c_int32),
+        ("max_seq_len", c_int32),
+        ("max_queries", c_int32),
+        ("flags", c_uint32),
+        ("seq_lens", c_void_p),
+        ("q_lens", c_void_p),
+        ("kv_stride_b", c_int64),
+        ("kv_stride_h", c_int64),
+        ("sc_stride_b", c_int64),
+        ("sc_stride_h", c_int64),
+        ("q_stride_b", c_int64),
+        ("q_stride_h", c_int64),
+        ("q_stride_t", c_int64),
+        ("o_stride_b", c_int64),
+        ("o_stride_h", c_int64),
+        ("o_stride_t", c_int64),
+        ("softmax_scale", c_float),
+    ]
+
+
 _SIGNATURES = {
     "solve": (None, [c_void_p] * 6 + [c_int] * 3),
     "kv_int8_split_launch": (c_int, [c_void_p] * 6 + [c_int] * 3 + [c_void_p, c_void_p]),
@@ -138,6 +165,8 @@ _SIGNATURES = {
     "kvd_mgpu_p2p_workspace_size": (c_size_t, [ctypes.POINTER(DecodeDesc)]),
     "kvd_mgpu_p2p_seq_split_decode": (c_int, [c_void_p, ctypes.POINTER(DecodeDesc)] + [c_void_p] * 6
                                       + [c_void_p, c_size_t, c_void_p]),
+    "kvd_prefill_workspace_size": (c_size_t, [ctypes.POINTER(PrefillDesc)]),
+    "kvd_prefill_launch": (c_int, [ctypes.POINTER(PrefillDesc)] + [c_void_p] * 7 + [c_size_t, c_void_p]),
     "kvd_paged_workspace_size": (c_size_t, [ctypes.POINTER(PagedDesc)]),
     "kvd_paged_decode_launch": (c_int, [ctypes.POINTER(PagedDesc)] + [c_void_p] * 7 + [c_size_t, c_void_p]),
     "kvd_paged_append_int8_launch": (c_int, [ctypes.POINTER(PagedDesc), c_void_p, c_void_p, c_int64, c_int64]
@@ -361,6 +390,47 @@ def append_decode(k_new, v_new, q, k, v, ks, vs, seq_lens, out=None, workspace=N
                                         k_new.stride(1), _ptr(q), _ptr(k), _ptr(v), _ptr(ks), _ptr(vs), _ptr(out),
                                         _ptr(workspace), workspace.numel(), _stream(stream))
     _check(rc, "kvd_append_decode_launch")
+    return out
+
+
+def make_prefill_desc(q, k, ks, out, seq_lens=None, q_lens=None, softmax_scale: float = 0.0) -> PrefillDesc:
+    """Descriptor for q [B,Hq,Lq,D], k/v [B,Hkv,cap,D] int8, ks/vs [B,Hkv,cap], out [B,Hq,Lq,D]."""
+    B, Hq, Lq, D = q.shape
+    Bk, Hkv, cap, Dk = k.shape
+    if Bk != B or Dk != D or Hq % Hkv or tuple(out.shape) != (B, Hq, Lq, D):
+        raise ValueError(f"shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} out{tuple(out.shape)}")
+    if k.stride(3) != 1 or k.stride(2) != D or ks.stride(2) != 1 or q.stride(3) != 1 or out.stride(3) != 1:
+        raise ValueError("token rows must be contiguous")
+    d = PrefillDesc()
+    d.batch, d.num_q_heads, d.num_kv_heads, d.head_dim = B, Hq, Hkv, D
+    d.max_seq_len, d.max_queries = cap, Lq
+    d.flags = dtype_flags(q, out)
+    d.seq_lens, d.q_lens = _ptr(seq_lens), _ptr(q_lens)
+    d.kv_stride_b, d.kv_stride_h = k.stride(0), k.stride(1)
+    d.sc_stride_b, d.sc_stride_h = ks.stride(0), ks.stride(1)
+    d.q_stride_b, d.q_stride_h, d.q_stride_t = q.stride(0), q.stride(1), q.stride(2)
+    d.o_stride_b, d.o_stride_h, d.o_stride_t = out.stride(0), out.stride(1), out.stride(2)
+    d.softmax_scale = softmax_scale
+    return d
+
+
+def prefill(q, k, v, ks, vs, seq_lens=None, q_lens=None, out=None, softmax_scale: float = 0.0, out_dtype=None,
+            workspace=None, stream=None):
+    """Causal prefill attention over the INT8 cache; q [B,Hq,Lq,D] holds the last q_lens[b]
+    (default Lq) of the seq_lens[b] (default cap) cached tokens. Returns out [B,Hq,Lq,D]."""
+    import torch
+
+    if out is None:
+        out = torch.empty(q.shape, dtype=out_dtype or torch.float32, device=q.device)
+    if v.stride() != k.stride() or vs.stride() != ks.stride():
+        raise ValueError("K/V and k_scale/v_scale must share strides")
+    desc = make_prefill_desc(q, k, ks, out, seq_lens, q_lens, softmax_scale)
+    if workspace is None:
+        workspace = torch.empty(max(int(lib().kvd_prefill_workspace_size(ctypes.byref(desc))), 1),
+                                dtype=torch.uint8, device=q.device)
+    rc = lib().kvd_prefill_launch(ctypes.byref(desc), _ptr(q), _ptr(k), _ptr(v), _ptr(ks), _ptr(vs), _ptr(out),
+                                  _ptr(workspace), workspace.numel(), _stream(stream))
+    _check(rc, "kvd_prefill_launch")
     return out
 
 

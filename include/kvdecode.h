@@ -231,6 +231,36 @@ cudaError_t kvd_append_decode_launch(const kvd_decode_desc* desc,
                                      const void* Q, int8_t* K, int8_t* V, float* k_scale, float* v_scale,
                                      void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------ */
+/* Causal prefill over the INT8 cache (no reference counterpart: the         */
+/* reference's prefill attention, attention/, is fp32 with no KV cache)      */
+/* ------------------------------------------------------------------------ */
+
+/* The prompt's K/V are already in the cache (quantised by the append or row
+ * kernels): sequence b holds seq_lens[b] tokens and its queries are the last
+ * q_lens[b] of them (q_lens[b] <= seq_lens[b]). Query i sits at position
+ * seq_lens[b] - q_lens[b] + i and attends to tokens [0, position]:
+ *   out[b][h][i] = softmax_t((q . K[t]) * ks[t] * scale) . (V[t] * vs[t]), t <= position.
+ * Query rows i >= q_lens[b] are written as 0. */
+typedef struct kvd_prefill_desc {
+    int32_t batch, num_q_heads, num_kv_heads, head_dim;
+    int32_t max_seq_len;      /* cache capacity per sequence */
+    int32_t max_queries;      /* query rows per (b, head) in Q and out */
+    uint32_t flags;           /* KVD_FLAG_Q_*, KVD_FLAG_OUT_* */
+    const int32_t* seq_lens;  /* device [B] or NULL (max_seq_len each) */
+    const int32_t* q_lens;    /* device [B] or NULL (max_queries each) */
+    int64_t kv_stride_b, kv_stride_h;          /* token stride D */
+    int64_t sc_stride_b, sc_stride_h;          /* token stride 1 */
+    int64_t q_stride_b, q_stride_h, q_stride_t;
+    int64_t o_stride_b, o_stride_h, o_stride_t;
+    float softmax_scale;      /* <= 0 selects 1/sqrt(D) */
+} kvd_prefill_desc;
+
+size_t kvd_prefill_workspace_size(const kvd_prefill_desc* desc);
+cudaError_t kvd_prefill_launch(const kvd_prefill_desc* desc, const void* Q, const int8_t* K, const int8_t* V,
+                               const float* k_scale, const float* v_scale, void* out,
+                               void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* Quantise `rows` contiguous fp32 rows of `dim` values (row stride x_stride
  * floats) to codes (row stride code_stride bytes) and one scale per row, with
  * the same rule as kvd_append_int8_launch. */

@@ -181,6 +181,41 @@ void kvo_decode_f64(const kvo_layout* L, const float* Q, const int8_t* K, const 
     }
 }
 
+void kvo_prefill_f64(int B, int Hq, int Hkv, int Lq, int cap, int D, const int32_t* seq_lens,
+                     const int32_t* q_lens, const float* Q, const int8_t* K, const int8_t* V,
+                     const float* k_scale, const float* v_scale, double softmax_scale, double* out) {
+    kvo_layout L;
+    memset(&L, 0, sizeof(L));
+    L.batch = B; L.num_q_heads = Hq; L.num_kv_heads = Hkv; L.head_dim = D; L.max_seq_len = cap;
+    L.kv_stride_b = (int64_t)Hkv * cap * D; L.kv_stride_h = (int64_t)cap * D;
+    L.sc_stride_b = (int64_t)Hkv * cap; L.sc_stride_h = cap;
+    L.q_stride_b = (int64_t)Hq * Lq * D; L.q_stride_h = (int64_t)Lq * D;
+    L.softmax_scale = softmax_scale;
+#pragma omp parallel
+    {
+        double* s = (double*)malloc(sizeof(double) * (size_t)(cap > 0 ? cap : 1));
+        double* rec = (double*)malloc(sizeof(double) * (size_t)(D + 2));
+#pragma omp for schedule(dynamic, 1)
+        for (int64_t u = 0; u < (int64_t)B * Hq * Lq; ++u) {
+            const int i = (int)(u % Lq), hq = (int)((u / Lq) % Hq), b = (int)(u / ((int64_t)Lq * Hq));
+            double* o = out + u * D;
+            const int ql = q_lens ? q_lens[b] : Lq;
+            int len = seq_lens ? seq_lens[b] : cap;
+            if (len > cap) len = cap;
+            const int pos = len - ql + i;  /* the query's own position */
+            if (i >= ql || pos < 0) {
+                for (int d = 0; d < D; ++d) o[d] = 0.0;
+                continue;
+            }
+            head_partial_f64(&L, Q + (int64_t)i * D, K, V, k_scale, v_scale, b, hq, 0, pos + 1, rec, s);
+            const double l = rec[1];
+            for (int d = 0; d < D; ++d) o[d] = l > 0.0 ? rec[2 + d] / l : 0.0;
+        }
+        free(rec);
+        free(s);
+    }
+}
+
 void kvo_partials_f64(const kvo_layout* L, const float* Q, const int8_t* K, const int8_t* V,
                       const float* k_scale, const float* v_scale,
                       int32_t t_begin, int32_t t_end, double* part) {

@@ -65,6 +65,15 @@ void kvo_cpu_reference_f32(const float* Q, const int8_t* K, const int8_t* V,
 void kvo_decode_f64(const kvo_layout* L, const float* Q, const int8_t* K, const int8_t* V,
                     const float* k_scale, const float* v_scale, double* out, int num_threads);
 
+/* FP64 causal prefill (no reference counterpart): q [B][Hq][Lq][D] fp32 dense,
+ * K/V [B][Hkv][cap][D], scales [B][Hkv][cap]. seq_lens[b] (or cap) tokens are in
+ * the cache; the queries are its last q_lens[b] (or Lq) tokens, so query i sits
+ * at position seq_lens[b] - q_lens[b] + i and attends to tokens [0, position].
+ * Rows i >= q_lens[b] are 0. out double [B][Hq][Lq][D]. */
+void kvo_prefill_f64(int B, int Hq, int Hkv, int Lq, int cap, int D, const int32_t* seq_lens,
+                     const int32_t* q_lens, const float* Q, const int8_t* K, const int8_t* V,
+                     const float* k_scale, const float* v_scale, double softmax_scale, double* out);
+
 /* FP64 split partial over tokens [t_begin, t_end) of every head (clipped to the
  * head's length). Record per (b, hq): m (natural-log domain max of scores),
  * l = sum exp(s - m), o[d] = sum exp(s - m) v[d] (unnormalised).

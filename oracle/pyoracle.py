@@ -63,6 +63,7 @@ def lib() -> ctypes.CDLL:
         _lib.kvo_decode_f64.argtypes = [ctypes.POINTER(Layout)] + [P] * 6 + [ctypes.c_int]
         _lib.kvo_partials_f64.argtypes = [ctypes.POINTER(Layout)] + [P] * 5 + [ctypes.c_int32] * 2 + [P]
         _lib.kvo_combine_f64.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
+        _lib.kvo_prefill_f64.argtypes = [ctypes.c_int] * 6 + [P] * 7 + [ctypes.c_double, P]
         _lib.kvo_fill_reference_pattern.argtypes = [P] * 5 + [ctypes.c_int] * 3
     return _lib
 
@@ -123,6 +124,23 @@ def decode_f64(q, K, V, ks, vs, seq_lens=None, softmax_scale: float = 0.0, threa
     L = _layout(q, K, ks, lens, softmax_scale)
     out = np.empty(q.shape, dtype=np.float64)
     lib().kvo_decode_f64(ctypes.byref(L), _p(q), _p(K), _p(V), _p(ks), _p(vs), _p(out), threads)
+    return out
+
+
+def prefill_f64(q, K, V, ks, vs, seq_lens=None, q_lens=None, softmax_scale: float = 0.0) -> np.ndarray:
+    """FP64 causal prefill: q [B,Hq,Lq,D] fp32, K/V [B,Hkv,cap,D] int8, ks/vs [B,Hkv,cap]; the
+    queries are the last q_lens[b] of seq_lens[b] cached tokens (query i attends to tokens up
+    to and including its own position). Rows past q_lens[b] are 0."""
+    q, K, V = (np.ascontiguousarray(a) for a in (q, K, V))
+    ks, vs = np.ascontiguousarray(ks, dtype=np.float32), np.ascontiguousarray(vs, dtype=np.float32)
+    B, Hq, Lq, D = q.shape
+    _, Hkv, cap, _ = K.shape
+    lens = None if seq_lens is None else np.ascontiguousarray(seq_lens, dtype=np.int32)
+    qls = None if q_lens is None else np.ascontiguousarray(q_lens, dtype=np.int32)
+    out = np.empty(q.shape, dtype=np.float64)
+    lib().kvo_prefill_f64(B, Hq, Hkv, Lq, cap, D, None if lens is None else _p(lens),
+                          None if qls is None else _p(qls), _p(q), _p(K), _p(V), _p(ks), _p(vs),
+                          ctypes.c_double(softmax_scale), _p(out))
     return out
 
 
