@@ -37,6 +37,7 @@
 #include "kvd_common.cuh"
 #include "kvd_decode.cuh"
 #include "kvd_quant.cuh"
+#include "kvd_tc.cuh"
 
 namespace kvd {
 
@@ -115,99 +116,6 @@ struct GqaCfg {
     static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
-// ---------------------------------------------------------- PTX wrappers
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                            uint64_t* bar, uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cta.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;"
-        ::"r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(policy)
-        : "memory");
-}
-
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                 ::"r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void fence_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// D[tmem] (+)= A[smem desc] x B[smem desc], int8 x int8 -> int32.
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                       bool accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate ? 1u : 0u)
-        : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                 ::"r"(smem_u32(bar)) : "memory");
-}
-
-// 32 consecutive TMEM columns of this warp's lane quarter -> 32 registers.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_wait_ld() {
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Shared-memory matrix descriptor (tcgen05): start, leading/stride byte
-// offsets (16-byte units), version 1, base offset 0, layout type.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
-                                              uint32_t layout) {
-    uint64_t d = 0;
-    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-    d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
-    d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
-    d |= static_cast<uint64_t>(1u) << 46;  // version
-    d |= static_cast<uint64_t>(layout & 7u) << 61;
-    return d;
-}
-constexpr uint32_t kLayoutNone = 0, kLayoutSw128 = 2;
-
-// Instruction descriptor, kind::i8: int32 accumulator, A/B signedness and
-// majorness, N and M.
-__host__ __device__ constexpr uint32_t idesc_i8(bool a_signed, bool b_signed, bool a_mn, bool b_mn, int N, int M) {
-    return (2u << 4) | ((a_signed ? 1u : 0u) << 7) | ((b_signed ? 1u : 0u) << 10) | ((a_mn ? 1u : 0u) << 15) |
-           ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
-}
-
 // Exact int32 -> fp32 for |v| < 2^22: 0x4B400000 + v is the float 1.5*2^23 + v.
 __device__ __forceinline__ float small_int_to_float(uint32_t v) {
     return __uint_as_float(0x4B400000u + v) - 12582912.0f;
@@ -225,12 +133,6 @@ __device__ __forceinline__ float pow2i(int e) {  // 2^e for e in [-126, 127]
     return __int_as_float((e + 127) << 23);
 }
 
-// 2^x on the special-function unit (relative error about 2^-22; 2^-inf = 0).
-__device__ __forceinline__ float ex2_fast(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
 
 // Smallest e with x < 2^e, for x >= 0 finite (subnormals and 0 give -126).
 __device__ __forceinline__ int exp_above(float x) {
@@ -1160,19 +1062,30 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // 128 bytes x 128 tokens, 128-byte swizzle (the canonical K-major operand
 // layout for K, and the MN-major one for V).
 bool make_kv_map(CUtensorMap* m, const int8_t* base, int B, int Hkv, int cap, int64_t kv_sb, int64_t kv_sh) {
+    return make_kv_map_rows(m, base, B, Hkv, cap, kv_sb, kv_sh, 128);
+}
+
+}  // namespace
+
+// As make_kv_map with a box of `rows` tokens (<= 256).
+bool make_kv_map_rows(void* map, const int8_t* base, int B, int Hkv, int cap, int64_t kv_sb, int64_t kv_sh,
+                      int rows) {
+    CUtensorMap* m = static_cast<CUtensorMap*>(map);
     auto fn = tensor_map_encoder();
     if (!fn) return false;
     const int64_t sh = kv_sh > 0 ? kv_sh : static_cast<int64_t>(cap) * 128;
     const int64_t sb = kv_sb > 0 ? kv_sb : sh * Hkv;
     cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(cap), static_cast<cuuint64_t>(Hkv), static_cast<cuuint64_t>(B)};
     cuuint64_t strides[3] = {128, static_cast<cuuint64_t>(sh), static_cast<cuuint64_t>(sb)};
-    cuuint32_t box[4] = {128, 128, 1, 1};
+    cuuint32_t box[4] = {128, static_cast<cuuint32_t>(rows), 1, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t*>(base), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
+
+namespace {
 
 // 4-D view {D bytes, block_size tokens, kv heads, blocks} of a paged K or V
 // pool, box of 128 bytes x min(block_size, 128) tokens, 128-byte swizzle. The
