@@ -349,6 +349,10 @@ extern "C" cudaError_t kvd_prefill_launch(const kvd_prefill_desc* desc, const vo
     if (!Q || !K || !V || !k_scale || !v_scale || !out) return cudaErrorInvalidValue;
     (void)workspace;
     (void)workspace_bytes;
+    if (prefill_tc_ok(*desc, K, V, k_scale, v_scale)) {  // head_dim 128: tensor-core kernel
+        e = launch_prefill_tc(*desc, Q, K, V, k_scale, v_scale, out, stream, &tl_launches);
+        if (e != cudaErrorNotSupported) return e;
+    }
     return launch_generic_prefill(*desc, Q, K, V, k_scale, v_scale, out, stream, &tl_launches);
 }
 

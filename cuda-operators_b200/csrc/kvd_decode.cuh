@@ -133,6 +133,9 @@ bool gqa_fused_append_ok(const kvd_decode_desc& d, size_t ws_bytes);
 // a box of 128 bytes x `rows` tokens, 128-byte swizzle (CUtensorMap* as void*).
 bool make_kv_map_rows(void* map, const int8_t* base, int B, int Hkv, int cap, int64_t kv_sb, int64_t kv_sh,
                       int rows);
+bool prefill_tc_ok(const kvd_prefill_desc& d, const int8_t* K, const int8_t* V, const float* ks, const float* vs);
+cudaError_t launch_prefill_tc(const kvd_prefill_desc& d, const void* Q, const int8_t* K, const int8_t* V,
+                              const float* ks, const float* vs, void* out, cudaStream_t st, int* launches);
 cudaError_t launch_generic_prefill(const kvd_prefill_desc& d, const void* Q, const int8_t* K, const int8_t* V,
                                    const float* ks, const float* vs, void* out, cudaStream_t st, int* launches);
 cudaError_t launch_paged_append(const kvd_paged_desc& d, const float* k_new, const float* v_new, int64_t new_sb,
