@@ -116,12 +116,35 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] x B[smem desc], bf16 x bf16 -> fp32 (kind::f16). A is
+// M rows (one per TMEM lane) by K, two 16-bit elements per 32-bit column, the
+// lower half holding the even k; a K = 16 step spans 8 columns.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                           bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+        : "memory");
+}
+
 // Instruction descriptor, kind::f16 with bf16 A and B and an fp32 accumulator:
-// D format F32 (1 at bit 4), A and B format BF16 (1 at bits 7 and 10), both
-// operands K-major, N and M.
-__host__ __device__ constexpr uint32_t idesc_bf16(int N, int M) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+// D format F32 (1 at bit 4), A and B format BF16 (1 at bits 7 and 10), A
+// K-major, B K-major or (b_mn) MN-major (bit 16), N and M.
+__host__ __device__ constexpr uint32_t idesc_bf16(int N, int M, bool b_mn = false) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) |
            (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// 16 registers -> 16 consecutive TMEM columns of this warp's lane quarter.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
 }
 
 // 32 registers -> 32 consecutive TMEM columns of this warp's lane quarter.
