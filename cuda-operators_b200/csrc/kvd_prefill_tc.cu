@@ -355,7 +355,12 @@ __device__ __forceinline__ void pf_converters(const PfParams& p, uint8_t* smem, 
 }
 
 // ------------------------------------------------------------------ MMA issuer
-// Lane 0 of warp 9, per item: S of the first two tiles, then per tile t the S
+// A bounded wait whose result is the same in every lane of the warp.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
+// Warp 9 (one elected lane issues), per item: S of the first two tiles, then per tile t the S
 // of tile t+2 (as soon as the softmax has read S(t), its buffer) and the PV of
 // tile t (once P(t) is written). S(j) = Qhi K^T + Qlo K^T into S buffer j&1
 // with Q from tensor memory; PV(j): O += Phi V + Plo V with P from P buffer
@@ -368,24 +373,24 @@ __device__ __forceinline__ void pf_mma(const PfParams& p, uint8_t* smem, uint32_
     constexpr uint32_t id_o = idesc_bf16(PD, PM, true);  // V is the MN-major B operand
     auto s_mma = [&](int64_t j) -> bool {
         const int jb = static_cast<int>(j & 1);
-        if (!mbar_wait(&bars[B_SREADY + jb], static_cast<uint32_t>((j >> 1) & 1))) return false;
+        if (!mbar_wait_warp(&bars[B_SREADY + jb], static_cast<uint32_t>((j >> 1) & 1))) return false;
         tc_fence_after();
         const uint64_t kd = smem_desc(smem_u32(smem + OFF_KB + jb * 16384), 16u, 1024u, kLayoutSw128);
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
 #pragma unroll
             for (int kk = 0; kk < PD / 16; ++kk)  // 16 dims: 32 bytes within a row, 64-dim atoms 8 KB apart
-                mma_f16_ts(tmem + jb * PT, tmem + COL_Q + 64u * half + 8u * kk,
+                mma_f16_ts_warp(tmem + jb * PT, tmem + COL_Q + 64u * half + 8u * kk,
                            kd + (((kk >> 2) * 8192u + (kk & 3) * 32u) >> 4), id_s, half > 0 || kk > 0);
         }
-        mma_commit(&bars[B_SDONE + jb]);
+        mma_commit_warp(&bars[B_SDONE + jb]);
         return true;
     };
     auto pv_mma = [&](int64_t j, bool first, int ni) -> bool {
         const int jb = static_cast<int>(j & 1);
         const uint32_t par = static_cast<uint32_t>((j >> 1) & 1);
-        if (!mbar_wait(&bars[B_PVREADY + jb], par)) return false;
-        if (first && ni > 0 && !mbar_wait(&bars[B_OREAD], static_cast<uint32_t>((ni - 1) & 1))) return false;
+        if (!mbar_wait_warp(&bars[B_PVREADY + jb], par)) return false;
+        if (first && ni > 0 && !mbar_wait_warp(&bars[B_OREAD], static_cast<uint32_t>((ni - 1) & 1))) return false;
         tc_fence_after();
         // 16 tokens = 2 groups of 8 token rows (SBO 1024); dims 64-127 one atom on (LBO 8192)
         const uint64_t vd = smem_desc(smem_u32(smem + OFF_VB + jb * 16384), 8192u, 1024u, kLayoutSw128);
@@ -394,10 +399,10 @@ __device__ __forceinline__ void pf_mma(const PfParams& p, uint8_t* smem, uint32_
         for (int half = 0; half < 2; ++half) {
 #pragma unroll
             for (int kk = 0; kk < PT / 16; ++kk)
-                mma_f16_ts(tmem + COL_O, pa + 32u * half + 8u * kk, vd + (2048u * kk >> 4), id_o,
+                mma_f16_ts_warp(tmem + COL_O, pa + 32u * half + 8u * kk, vd + (2048u * kk >> 4), id_o,
                            !(first && half == 0 && kk == 0));
         }
-        mma_commit(&bars[B_PVDONE + jb]);
+        mma_commit_warp(&bars[B_PVDONE + jb]);
         return true;
     };
     int64_t j0 = 0;
@@ -405,14 +410,14 @@ __device__ __forceinline__ void pf_mma(const PfParams& p, uint8_t* smem, uint32_
     for (int it = pf_next(p, blockIdx.x); it < p.n_items; it = pf_next(p, it + p.grid), ++ni) {
         const PfItem I = pf_item(p, it);
         const int nt = I.ntiles;
-        if (!mbar_wait(&bars[B_QFULL], static_cast<uint32_t>(ni & 1))) return;
+        if (!mbar_wait_warp(&bars[B_QFULL], static_cast<uint32_t>(ni & 1))) return;
         for (int t = 0; t < min(2, nt); ++t)
             if (!s_mma(j0 + t)) return;
-        if (nt <= 2) mma_commit(&bars[B_QEMPTY]);
+        if (nt <= 2) mma_commit_warp(&bars[B_QEMPTY]);
         for (int t = 0; t < nt; ++t) {
             if (t + 2 < nt) {
                 if (!s_mma(j0 + t + 2)) return;
-                if (t + 3 == nt) mma_commit(&bars[B_QEMPTY]);  // the item's last S: the queries may be replaced
+                if (t + 3 == nt) mma_commit_warp(&bars[B_QEMPTY]);  // the item's last S: the queries may be replaced
             }
             if (!pv_mma(j0 + t, t == 0, ni)) return;
         }
@@ -646,12 +651,10 @@ __global__ void __launch_bounds__(P_THREADS, 1) prefill_tc_kernel(const __grid_c
     } else if (warp == 8) {
         if (lane == 0) pf_producer(&kmap, &vmap, p, smem);
     } else {
-        if (lane == 0) {
-            pf_mma(p, smem, tmem);
-            mma_commit(&bars[B_DRAIN]);  // arrives once every MMA issued above has completed
-            mbar_wait(&bars[B_DRAIN], 0);
-            mbar_wait(&bars[B_DONE], 0);  // the softmax warps have finished with tensor memory
-        }
+        pf_mma(p, smem, tmem);
+        mma_commit_warp(&bars[B_DRAIN]);  // arrives once every MMA issued above has completed
+        mbar_wait(&bars[B_DRAIN], 0);
+        mbar_wait(&bars[B_DONE], 0);  // the softmax warps have finished with tensor memory
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem, P_TMEM_COLS);

@@ -129,6 +129,29 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
         : "memory");
 }
 
+// As mma_f16_ts and mma_commit, executed by a whole warp with warp-uniform
+// operands: one elected lane issues. Keeping the operands uniform lets the
+// compiler hold them in uniform registers, so back-to-back MMAs issue without
+// per-instruction register moves.
+__device__ __forceinline__ void mma_f16_ts_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                                bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t"
+        "elect.sync r|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_warp(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
+        "elect.sync r|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}"
+        ::"r"(smem_u32(bar)) : "memory");
+}
+
 // Instruction descriptor, kind::f16 with bf16 A and B and an fp32 accumulator:
 // D format F32 (1 at bit 4), A and B format BF16 (1 at bits 7 and 10), A
 // K-major, B K-major or (b_mn) MN-major (bit 16), N and M.
