@@ -477,7 +477,7 @@ __device__ __forceinline__ void pf_softmax(const PfParams& p, uint8_t* smem, uin
         const int pos = I.L - I.ql + i;                // this query's own position
         const int pos_lo = I.L - I.ql + I.qb * p.QPB;  // the block's first query
         float m = -INFINITY;
-        float2 l2 = make_float2(0.f, 0.f);
+        float2 lp[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // row sum, 4 independent chains
         for (int tt = 0; tt < I.ntiles; ++tt, ++j) {
             const int sb = static_cast<int>(j & 1), c = static_cast<int>(j % PSC), t0 = tt * PT;
             // ---- scores of tile j
@@ -495,7 +495,7 @@ __device__ __forceinline__ void pf_softmax(const PfParams& p, uint8_t* smem, uin
             const float4* vs4 = ks4 + 16;
             // the causal mask only matters on tiles that reach past the block's first query; masked
             // scores become -inf (the weights loop below has no branch: 2^-inf = 0)
-            float tmax = -INFINITY;
+            float tm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // 4 independent chains
             if (t0 + PT - 1 > pos_lo) {
                 const int lim = valid ? pos - t0 : -1;  // tokens c <= lim are visible to this row
 #pragma unroll
@@ -511,7 +511,7 @@ __device__ __forceinline__ void pf_softmax(const PfParams& p, uint8_t* smem, uin
                     sr[4 * k + 1] = __float_as_uint(v1);
                     sr[4 * k + 2] = __float_as_uint(v2);
                     sr[4 * k + 3] = __float_as_uint(v3);
-                    tmax = fmax3(fmax3(tmax, v0, v1), v2, v3);
+                    tm[k & 3] = fmax3(fmax3(tm[k & 3], v0, v1), v2, v3);
                 }
             } else {
 #pragma unroll
@@ -525,9 +525,10 @@ __device__ __forceinline__ void pf_softmax(const PfParams& p, uint8_t* smem, uin
                     sr[4 * k + 1] = __float_as_uint(va.y);
                     sr[4 * k + 2] = __float_as_uint(vb.x);
                     sr[4 * k + 3] = __float_as_uint(vb.y);
-                    tmax = fmax3(fmax3(tmax, va.x, va.y), vb.x, vb.y);
+                    tm[k & 3] = fmax3(fmax3(tm[k & 3], va.x, va.y), vb.x, vb.y);
                 }
             }
+            const float tmax = fmaxf(fmaxf(tm[0], tm[1]), fmaxf(tm[2], tm[3]));
             // ---- lazy rescale: the running max may trail by up to 8
             const bool need = m != -INFINITY && tmax > m + 8.f;
             if (__any_sync(0xffffffffu, need)) {
@@ -545,8 +546,8 @@ __device__ __forceinline__ void pf_softmax(const PfParams& p, uint8_t* smem, uin
                     tmem_st32(lane_base + COL_O + 32 * cc, o);
                 }
                 tmem_wait_st();
-                l2.x *= f;
-                l2.y *= f;
+                lp[0] = __fmul2_rn(lp[0], make_float2(f, f));
+                lp[1] = __fmul2_rn(lp[1], make_float2(f, f));
             }
             if (need || (m == -INFINITY && tmax != -INFINITY)) m = tmax;
             // ---- P buffer sb is free once PV(j-2) has completed
@@ -563,7 +564,7 @@ __device__ __forceinline__ void pf_softmax(const PfParams& p, uint8_t* smem, uin
                     const int cp = 16 * q + k;  // token pair
                     const float2 d = __fadd2_rn(make_float2(__uint_as_float(sr[2 * cp]), __uint_as_float(sr[2 * cp + 1])), nm);
                     const float2 pp = make_float2(ex2_fast(d.x), ex2_fast(d.y));
-                    l2 = __fadd2_rn(l2, pp);
+                    lp[k & 1] = __fadd2_rn(lp[k & 1], pp);
                     const float4 vq = vs4[cp >> 1];  // scales in the ring are always finite
                     const float2 w = __fmul2_rn(pp, (cp & 1) ? make_float2(vq.z, vq.w) : make_float2(vq.x, vq.y));
                     const uint32_t h = bf16x2(w.x, w.y);
@@ -586,7 +587,7 @@ __device__ __forceinline__ void pf_softmax(const PfParams& p, uint8_t* smem, uin
             if (tt == I.ntiles - 1) {
                 if (!mbar_wait(&bars[B_PVDONE + sb], static_cast<uint32_t>((j >> 1) & 1))) return;
                 tc_fence_after();
-                const float l = l2.x + l2.y;
+                const float l = (lp[0].x + lp[0].y) + (lp[1].x + lp[1].y);
                 const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
                 for (int cc = 0; cc < PD / 32; ++cc) {
