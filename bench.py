@@ -455,6 +455,45 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def run_prefill(args) -> None:
+    """Side measurement (not the headline): causal prefill over an INT8 cache.
+    --prefill B,Hq,Hkv,L,Lq: B sequences of L cached tokens whose last Lq are
+    the queries; fp32 Q and output; seeded random codes and scales. Prints one
+    JSON line with attention TFLOP/s (4*D FLOPs per visible query-token pair;
+    the MMAs do twice that, hi + lo operands)."""
+    import torch
+    import kvdecode as kvd
+
+    B, Hq, Hkv, L, Lq = (int(x) for x in args.prefill.split(","))
+    D = 128
+    dev = "cuda:0"
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    K = torch.randint(-127, 128, (B, Hkv, L, D), dtype=torch.int8, device=dev, generator=g)
+    V = torch.randint(-127, 128, (B, Hkv, L, D), dtype=torch.int8, device=dev, generator=g)
+    ks = torch.rand(B, Hkv, L, device=dev, generator=g) * 0.02
+    vs = torch.rand(B, Hkv, L, device=dev, generator=g) * 0.02
+    q = torch.randn(B, Hq, Lq, D, device=dev, generator=g)
+    out = torch.empty(B, Hq, Lq, D, device=dev)
+    for _ in range(args.warmup):
+        kvd.prefill(q, K, V, ks, vs, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        kvd.prefill(q, K, V, ks, vs, out=out)
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) / args.steps * 1e3
+    if kvd.device_status() != kvd.KVD_STATUS_OK:
+        raise RuntimeError("prefill kernel reported a bad status")
+    pairs = B * Hq * (Lq * (L - Lq) + Lq * (Lq + 1) / 2)
+    print(json.dumps({"metric": "INT8 KV causal prefill: attention TFLOP/s", "value": pairs * D * 4 / us / 1e6,
+                      "unit": "TFLOP/s", "us_per_step": us, "steps": args.steps, "warmup": args.warmup,
+                      "dtype": "f32 in, bf16 hi+lo MMA operands, f32 accumulate", "data": "synthetic",
+                      "config": {"workload": "prefill", "batch": B, "q_heads": Hq, "kv_heads": Hkv,
+                                 "cache_tokens": L, "queries": Lq, "head_dim": D}}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -474,10 +513,14 @@ def main() -> None:
                     help="config 4: append kernel then decode (default: one fused append+decode launch)")
     ap.add_argument("--paged", type=int, default=0, metavar="BS",
                     help="decode through the paged-cache entry point with BS-token blocks (0: dense cache)")
+    ap.add_argument("--prefill", default="", metavar="B,HQ,HKV,L,LQ",
+                    help="time the causal prefill kernel on this shape instead (a side measurement)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.prefill:
+        run_prefill(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
