@@ -360,9 +360,9 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
     return __all_sync(0xffffffffu, mbar_wait(bar, parity));
 }
 
-// Warp 9 (one elected lane issues), per item: S of the first two tiles, then per tile t the S
-// of tile t+2 (as soon as the softmax has read S(t), its buffer) and the PV of
-// tile t (once P(t) is written). S(j) = Qhi K^T + Qlo K^T into S buffer j&1
+// Warp 9 (one elected lane issues), per item: S of the first two tiles, then per tile t the PV
+// of tile t (once P(t) is written) and the S of tile t+2 (its buffer was read by
+// the softmax at tile t). S(j) = Qhi K^T + Qlo K^T into S buffer j&1
 // with Q from tensor memory; PV(j): O += Phi V + Plo V with P from P buffer
 // j&1 (overwriting O at an item's first tile, after the softmax has read the
 // previous item's O). An item's PVs all precede the next item's first S, which
@@ -415,11 +415,13 @@ __device__ __forceinline__ void pf_mma(const PfParams& p, uint8_t* smem, uint32_
             if (!s_mma(j0 + t)) return;
         if (nt <= 2) mma_commit_warp(&bars[B_QEMPTY]);
         for (int t = 0; t < nt; ++t) {
+            if (!pv_mma(j0 + t, t == 0, ni)) return;
+            // S(t+2) after PV(t): its completion (SDONE) then also means that PV(t) has read P
+            // buffer t&1, which the softmax rewrites at tile t+2
             if (t + 2 < nt) {
                 if (!s_mma(j0 + t + 2)) return;
                 if (t + 3 == nt) mma_commit_warp(&bars[B_QEMPTY]);  // the item's last S: the queries may be replaced
             }
-            if (!pv_mma(j0 + t, t == 0, ni)) return;
         }
         j0 += nt;
     }
@@ -550,8 +552,7 @@ __device__ __forceinline__ void pf_softmax(const PfParams& p, uint8_t* smem, uin
                 lp[1] = __fmul2_rn(lp[1], make_float2(f, f));
             }
             if (need || (m == -INFINITY && tmax != -INFINITY)) m = tmax;
-            // ---- P buffer sb is free once PV(j-2) has completed
-            if (j >= 2 && !mbar_wait(&bars[B_PVDONE + sb], static_cast<uint32_t>(((j >> 1) - 1) & 1))) return;
+            // (P buffer sb is free: PV(j-2) was issued before S(j), whose completion was awaited above)
             // ---- weights w = 2^(s - m) * v_scale as bf16 hi + lo, 32 tokens at a time
             const uint32_t pcol = lane_base + COL_P + static_cast<uint32_t>(sb) * 64u;
             const float me = m == -INFINITY ? 0.f : m;  // a row with every score masked so far: all weights 0

@@ -77,6 +77,9 @@ PREFILL_CASES = [
     (1, 16, 1, 33, 1000, 128, [1000], None),                  # GQA 16
     (2, 4, 4, 50, 300, 64, [300, 120], [50, 20]),            # head_dim 64
     (1, 6, 2, 17, 90, 96, None, None),                       # head_dim 96
+    (2, 4, 2, 70, 150, 128, [150, 0], [70, 0]),              # GQA 2, an empty sequence
+    (3, 8, 8, 40, 100, 128, [100, 37, 64], [0, 37, 10]),     # a sequence without queries, ragged tails
+    (1, 16, 8, 257, 1100, 128, [1100], [257]),               # GQA 2, queries past two 128-row blocks
 ]
 
 
