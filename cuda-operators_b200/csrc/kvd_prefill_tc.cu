@@ -7,7 +7,7 @@
 // group share every K/V tile. The item walks 64-token tiles of its causal
 // prefix:
 //   * a producer thread loads the INT8 K and V tiles (TMA, 128-byte swizzle)
-//     into a 4-deep ring and both scale windows into an 8-deep ring of their
+//     into a 6-deep ring and both scale windows into an 8-deep ring of their
 //     own;
 //   * a converter warpgroup widens each INT8 tile to bf16 (codes are exact in
 //     bf16) in one row-per-token, 128-byte-swizzled layout that is the K-major
@@ -16,11 +16,12 @@
 //     sign flip, a byte permute that builds the float 2^23 + 128 + code, one
 //     packed add and a byte permute of the upper halves. It also writes each
 //     item's queries, scaled by softmax_scale*log2(e), as two bf16 terms
-//     (hi + lo, about 16 significant bits) into the A operand;
-//   * one thread issues the MMAs (kind::f16, M = 128, fp32 accumulators in
-//     tensor memory): S(j) = Qhi K^T + Qlo K^T (N = 64) into one of two S
-//     buffers, then O += Phi V + Plo V for tile j-1 with P read from tensor
-//     memory (A operand in TMEM, N = 128);
+//     (hi + lo, about 16 significant bits) into tensor memory (the A operand
+//     of S);
+//   * one elected lane of the MMA warp issues the MMAs (kind::f16, M = 128,
+//     fp32 accumulators in tensor memory, A operands read from tensor memory):
+//     S(j) = Qhi K^T + Qlo K^T (N = 64) into one of two S buffers, two tiles
+//     ahead of O += Phi V + Plo V (N = 128);
 //   * a softmax warpgroup owns one query row per thread (= TMEM lane): scores
 //     times the token's k_scale, the causal mask (only on the tiles that
 //     reach the block's first query), a lazily rescaled online softmax in base
