@@ -340,8 +340,11 @@ def run_ours(args) -> None:
         step()
 
     # Decode steps are replayed from a CUDA graph (G steps per graph) so that
-    # host launch overhead does not hide the device time of small configs.
-    G = 10 if args.steps % 10 == 0 and not args.no_graph and not seqsplit else 1
+    # host launch overhead does not hide the device time of small configs. The
+    # sequence split is captured with the peer-store exchange only (its kernel
+    # counts epochs on the device); the NCCL and torch exchanges launch eagerly.
+    graphable = not seqsplit or args.exchange == "p2p"
+    G = 10 if args.steps % 10 == 0 and not args.no_graph and graphable else 1
     if G > 1:
         graph = torch.cuda.CUDAGraph()
         torch.cuda.synchronize()
