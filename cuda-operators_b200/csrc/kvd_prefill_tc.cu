@@ -109,15 +109,12 @@ __device__ __forceinline__ PfItem pf_item(const PfParams& p, int it) {
     I.b = rem / p.Hkv;
     I.hk = rem - I.b * p.Hkv;
     I.L = p.seq_lens ? min(max(0, __ldg(p.seq_lens + I.b)), p.S) : p.S;
+    // query i sits at position L - ql + i; with more queries than tokens the first rows
+    // would sit before position 0 and are written as zeros
     I.ql = p.q_lens ? min(max(0, __ldg(p.q_lens + I.b)), p.Lq) : p.Lq;
-    I.ql = min(I.ql, I.L);
     const int q0 = I.qb * p.QPB;
-    if (q0 >= I.ql) {
-        I.ntiles = 0;
-    } else {
-        const int ntok = I.L - I.ql + min(I.ql, q0 + p.QPB);  // tokens up to the block's last query
-        I.ntiles = (ntok + PT - 1) / PT;
-    }
+    const int ntok = I.L - I.ql + min(I.ql, q0 + p.QPB);  // tokens up to the block's last query
+    I.ntiles = q0 < I.ql && ntok > 0 ? (ntok + PT - 1) / PT : 0;
     return I;
 }
 
@@ -476,8 +473,8 @@ __device__ __forceinline__ void pf_softmax(const PfParams& p, uint8_t* smem, uin
             continue;
         }
         const int i = I.qb * p.QPB + r / p.G;
-        const bool valid = i < I.ql;
         const int pos = I.L - I.ql + i;                // this query's own position
+        const bool valid = i < I.ql && pos >= 0;
         const int pos_lo = I.L - I.ql + I.qb * p.QPB;  // the block's first query
         float m = -INFINITY;
         float2 lp[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // row sum, 4 independent chains

@@ -241,7 +241,8 @@ cudaError_t kvd_append_decode_launch(const kvd_decode_desc* desc,
  * q_lens[b] of them (q_lens[b] <= seq_lens[b]). Query i sits at position
  * seq_lens[b] - q_lens[b] + i and attends to tokens [0, position]:
  *   out[b][h][i] = softmax_t((q . K[t]) * ks[t] * scale) . (V[t] * vs[t]), t <= position.
- * Query rows i >= q_lens[b] are written as 0. */
+ * Query rows i >= q_lens[b], and rows whose position would be negative (more
+ * queries than tokens), are written as 0. */
 typedef struct kvd_prefill_desc {
     int32_t batch, num_q_heads, num_kv_heads, head_dim;
     int32_t max_seq_len;      /* cache capacity per sequence */

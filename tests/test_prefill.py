@@ -80,6 +80,8 @@ PREFILL_CASES = [
     (2, 4, 2, 70, 150, 128, [150, 0], [70, 0]),              # GQA 2, an empty sequence
     (3, 8, 8, 40, 100, 128, [100, 37, 64], [0, 37, 10]),     # a sequence without queries, ragged tails
     (1, 16, 8, 257, 1100, 128, [1100], [257]),               # GQA 2, queries past two 128-row blocks
+    (2, 8, 4, 140, 200, 128, [30, 200], [140, 20]),          # more queries than tokens: leading rows are 0
+    (1, 4, 4, 20, 40, 64, [12], [20]),                       # the same on the generic kernel
 ]
 
 
