@@ -404,7 +404,7 @@ def run_ours(args) -> None:
     # so that host launch overhead does not stand in for the end-to-end time of small configs.
     run_e2e = e2e_step
     n_e2e = max(10, args.steps // 4)
-    if G > 1:
+    if G > 1 and world == 1:
         e2e_graph = torch.cuda.CUDAGraph()
         torch.cuda.synchronize()
         with torch.cuda.graph(e2e_graph):
@@ -421,7 +421,8 @@ def run_ours(args) -> None:
             raise RuntimeError("the end-to-end graph does not reproduce the step's output")
         run_e2e = e2e_graph.replay
         n_e2e = max(1, n_e2e // G)
-    e2e_ms = timed(run_e2e, n_e2e) / (G if G > 1 else 1)
+    G_e2e = G if run_e2e is not e2e_step else 1
+    e2e_ms = timed(run_e2e, n_e2e) / G_e2e
 
     peak, peak_kind = measured_peak()
     per_gpu_gbs = nbytes / (ms * 1e-3) / 1e9
@@ -458,7 +459,7 @@ def run_ours(args) -> None:
                                   else " after the append kernel") if cfg.append else "")},
         "clocks": clk.summary(),
         "e2e": {"value": e2e_gbs, "unit": "GB/s", "ms_per_step": e2e_ms,
-                "launch": f"CUDA graph of {G} steps, copies included" if G > 1 else "direct launches",
+                "launch": f"CUDA graph of {G_e2e} steps, copies included" if G_e2e > 1 else "direct launches",
                 "h2d_bytes_per_step": int(q_host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4),
                 "call": ("kv_int8_split_launch" if flat else
                          "kvd_paged_decode_launch" if pool is not None else "kvd_decode_launch")},
