@@ -18,13 +18,17 @@ cudaError_t launch_quantize_rows(const float* x, int64_t rows, int dim, int64_t 
                                  int64_t code_stride, float* scales, int sms, cudaStream_t st);
 
 int device_sm_count() {
-    static int cache[64] = {};
+    static std::atomic<int> cache[kMaxDevices] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 1;
-    if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
+    const bool cached = dev >= 0 && dev < kMaxDevices;
+    if (cached) {
+        const int n = cache[dev].load(std::memory_order_relaxed);
+        if (n > 0) return n;
+    }
     int n = 0;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 1;
-    if (dev >= 0 && dev < 64) cache[dev] = n;
+    if (cached) cache[dev].store(n, std::memory_order_relaxed);
     return n;
 }
 
@@ -107,6 +111,12 @@ extern "C" cudaError_t kvd_decode_launch(const kvd_decode_desc* desc, const void
     if (!fast_path_ok(d, Q, K, V))
         return launch_generic(d, Q, K, V, k_scale, v_scale, out, workspace, workspace_bytes, stream,
                               &tl_launches);
+
+    // Small dense MHA problems (too few bytes to fill the GPU): one launch, a
+    // cluster of CTAs per head merging through distributed shared memory.
+    if (small_cluster_size(d) > 0)
+        return launch_small(d, static_cast<const float*>(Q), K, V, k_scale, v_scale, static_cast<float*>(out),
+                            stream, &tl_launches);
 
     // Grouped-query heads share every K/V tile: tensor-core kernel. MHA with
     // D=128 takes it too: the tensor cores do QK and PV, so the SMs spend far

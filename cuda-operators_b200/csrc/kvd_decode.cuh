@@ -2,13 +2,48 @@
 // units (split-KV flash decode on CUDA cores, combine, generic fallback).
 #pragma once
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
+#include <mutex>
 #include <cuda_runtime.h>
 
 #include "kvdecode.h"
 
 namespace kvd {
+
+// Device ordinals the library keeps per-device state for (kernel attributes,
+// cached SM counts); calls on higher ordinals return cudaErrorInvalidDevice.
+constexpr int kMaxDevices = 64;
+
+// Runs a set-up step (a kernel attribute) once per device, for the device
+// current on the calling thread. Thread-safe: concurrent first calls wait for
+// one another; a failed step is retried by the next call.
+class PerDeviceOnce {
+public:
+    template <class F>
+    cudaError_t run(F&& fn) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+        if (done_[dev].load(std::memory_order_acquire)) return cudaSuccess;
+        std::lock_guard<std::mutex> lock(mu_);
+        if (done_[dev].load(std::memory_order_relaxed)) return cudaSuccess;
+        e = fn();
+        if (e == cudaSuccess) done_[dev].store(true, std::memory_order_release);
+        return e;
+    }
+
+private:
+    std::mutex mu_;
+    std::atomic<bool> done_[kMaxDevices] = {};
+};
+
+// One-launch small-problem decode (kvd_small.cu): at most kSmallMaxCluster
+// CTAs (a thread-block cluster) per head, kSmallMaxSpan tokens per CTA.
+constexpr int kSmallMaxCluster = 8;
+constexpr int kSmallMaxSpan = 256;
 
 // Everything a decode kernel needs, passed by value.
 struct DecodeParams {
@@ -114,6 +149,9 @@ int device_sm_count();
 cudaError_t launch_plan(const int32_t* seq_lens, int B, int Hq, int tok, int cap, int32_t* prefix,
                         cudaStream_t st, int* launches);
 cudaError_t launch_splitkv(const DecodeParams& p, cudaStream_t st, int* launches);
+int small_cluster_size(const kvd_decode_desc& d);
+cudaError_t launch_small(const kvd_decode_desc& d, const float* Q, const int8_t* K, const int8_t* V,
+                         const float* ks, const float* vs, float* out, cudaStream_t st, int* launches);
 cudaError_t launch_generic(const kvd_decode_desc& d, const void* Q, const int8_t* K,
                            const int8_t* V, const float* ks, const float* vs, void* out,
                            void* ws, size_t ws_bytes, cudaStream_t st, int* launches,

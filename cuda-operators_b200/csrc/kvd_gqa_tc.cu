@@ -1133,16 +1133,12 @@ int gqa_split_count(const kvd_decode_desc& d) {
 template <int G>
 cudaError_t launch_gqa_g(const CUtensorMap& km, const CUtensorMap& vm, const GqaParams& p, cudaStream_t st) {
     using C = GqaCfg<G, kGqaNK, kGqaNV>;
-    static bool configured[64] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
     auto kern = gqa_tc_kernel<G, kGqaNK, kGqaNV, kGqaCtas>;
-    if (dev < 64 && !configured[dev]) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        configured[dev] = true;
-    }
+    static PerDeviceOnce once;
+    const cudaError_t e = once.run([kern] {
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    });
+    if (e != cudaSuccess) return e;
     kern<<<p.grid, C::THREADS, C::SMEM_BYTES, st>>>(km, vm, p);
     return cudaGetLastError();
 }

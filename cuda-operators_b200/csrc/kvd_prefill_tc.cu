@@ -701,15 +701,11 @@ cudaError_t launch_prefill_tc(const kvd_prefill_desc& d, const void* Q, const in
     const int qe = (d.flags & (KVD_FLAG_Q_BF16 | KVD_FLAG_Q_F16)) ? 8 : 4;  // elements per 16 bytes
     p.vec_q = (reinterpret_cast<uintptr_t>(Q) & 15) == 0 && d.q_stride_b % qe == 0 && d.q_stride_h % qe == 0 &&
               d.q_stride_t % qe == 0;
-    static bool configured[64] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    static PerDeviceOnce once;
+    cudaError_t e = once.run([] {
+        return cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
+    });
     if (e != cudaSuccess) return e;
-    if (dev < 64 && !configured[dev]) {
-        e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        configured[dev] = true;
-    }
     prefill_tc_kernel<<<p.grid, P_THREADS, P_SMEM_BYTES, st>>>(km, vm, p);
     e = cudaGetLastError();
     if (e == cudaSuccess) ++*launches;

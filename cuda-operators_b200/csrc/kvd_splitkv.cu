@@ -501,15 +501,11 @@ namespace {
 template <int D>
 cudaError_t launch_sk(const DecodeParams& p, cudaStream_t st, int* launches) {
     using C = SkCfg<D>;
-    static bool configured[64] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    static PerDeviceOnce once;
+    cudaError_t e = once.run([] {
+        return cudaFuncSetAttribute(splitkv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    });
     if (e != cudaSuccess) return e;
-    if (dev < 64 && !configured[dev]) {
-        e = cudaFuncSetAttribute(splitkv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        configured[dev] = true;
-    }
     splitkv_kernel<D><<<p.grid, C::THREADS, C::SMEM_BYTES, st>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;

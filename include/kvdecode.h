@@ -11,7 +11,9 @@
  * applied to V[h,t] * vs[h,t].
  *
  * All launches are asynchronous on the given stream (the default stream for
- * `solve`); the caller synchronises before reading results.
+ * `solve`); the caller synchronises before reading results. Calls are
+ * thread-safe (per-device one-time set-up is guarded); devices with an ordinal
+ * of 64 or more are not supported (cudaErrorInvalidDevice).
  */
 #ifndef KVDECODE_H
 #define KVDECODE_H
@@ -119,10 +121,12 @@ cudaError_t kvd_decode_launch(const kvd_decode_desc* desc,
  * serving loop that bans allocation on its hot path): its scratch lives in a
  * fixed KVD_NOALLOC_SCRATCH_BYTES array inside the library, held by every GPU
  * that loads the library until exit. Descriptors whose kvd_workspace_size()
- * exceeds the array are rejected with cudaErrorInvalidValue. The first call on
- * a device resolves the array's address (make it outside any stream capture).
- * All calls share the array: calls that overlap on the GPU race. Allocates
- * nothing. */
+ * exceeds the array are rejected with cudaErrorInvalidValue (long contexts do:
+ * 4 x 32 heads x 131,072 tokens needs 2.5 MB of split records). The first call
+ * in each CUDA context of a device (the first call, and the first after a
+ * cudaDeviceReset) resolves the array's address: make it outside any stream
+ * capture. All calls share the array: calls that overlap on the GPU race.
+ * Allocates nothing. */
 #define KVD_NOALLOC_SCRATCH_BYTES (512u * 1024u)
 cudaError_t kvd_decode_launch_noalloc(const kvd_decode_desc* desc,
                                       const void* Q, const int8_t* K, const int8_t* V,
