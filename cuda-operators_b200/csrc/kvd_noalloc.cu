@@ -13,15 +13,20 @@
 // Properties a caller must know:
 //  * Size: KVD_NOALLOC_SCRATCH_BYTES (512 KiB). A descriptor whose
 //    kvd_workspace_size() exceeds it is rejected with cudaErrorInvalidValue and
-//    one line on stderr; nothing is launched. On a B200 a dense decode needs
-//    about 312 KiB for head_dim 128, so the limit binds only for very large
-//    ragged batches or the generic (other head_dim) path.
+//    one line on stderr; nothing is launched. The size grows with the split
+//    records of long sequences: on a B200 a dense head_dim-128 decode of 4,096
+//    tokens fits (about 312 KiB), but long contexts do not -- 4 sequences x 32
+//    heads x 131,072 tokens plans 37 splits per head, 2.5 MB of records -- nor
+//    do very large ragged batches, whose plan arrays alone outgrow the array.
 //  * Memory: the array is a static __device__ object, so every GPU that loads
 //    this library holds 512 KiB for it until the process exits.
 //  * Set-up: the first call on each device (with that device current) looks
-//    up the array's device address with cudaGetSymbolAddress and caches it.
-//    That lookup may load the library's device code, so make the first call on
-//    a device outside any stream capture.
+//    up the array's device address with cudaGetSymbolAddress and caches it
+//    together with the unique id of the CUDA context it belongs to. A call in
+//    another context of that device (after cudaDeviceReset, or under a context
+//    the caller made current) looks the address up again. The lookup may load
+//    the library's device code, so make the first call on a device -- and the
+//    first one after a reset -- outside any stream capture.
 //  * Sharing: every call uses the same array and it keeps whatever the last
 //    call wrote. Nothing in it has to start at zero -- each call writes every
 //    record it later reads -- but two calls whose kernels overlap on the GPU
@@ -29,6 +34,8 @@
 //    scratch and produce wrong results. Issue them in order on one stream, or
 //    use kvd_decode_launch with a workspace per concurrent call.
 //  * It calls no cudaMalloc, cudaFree or other allocating routine.
+#include <cuda.h>
+
 #include <cstdio>
 #include <mutex>
 
@@ -40,11 +47,34 @@ namespace {
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[KVD_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
+struct NoallocSlot {
+    unsigned long long ctx_id;  // unique id of the context the address belongs to (0: none yet)
+    void* addr;
+};
 std::mutex g_noalloc_mutex;
-void* g_noalloc_addr[kMaxDevices] = {};
+NoallocSlot g_noalloc_slots[kMaxDevices] = {};
 
-// Device address of g_noalloc_scratch on the current device (host code sees
+// Unique id of the calling thread's current CUDA context (cuCtxGetId: ids are
+// never reused within a process), or 0 when none is current yet or the driver
+// lacks the call. Resolved through the runtime, so the library does not link
+// the driver library.
+unsigned long long current_context_id() {
+    using Fn = CUresult (*)(CUcontext, unsigned long long*);
+    static Fn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<Fn>(ptr);
+    });
+    unsigned long long id = 0;
+    if (!fn || fn(nullptr, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
+// Device address of g_noalloc_scratch in the current context (host code sees
 // only a host-side stand-in for the symbol; it must never be passed to a kernel).
 cudaError_t noalloc_scratch_address(void** out) {
     int dev = 0;
@@ -52,13 +82,16 @@ cudaError_t noalloc_scratch_address(void** out) {
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (g_noalloc_addr[dev] == nullptr) {
+    NoallocSlot& slot = g_noalloc_slots[dev];
+    const unsigned long long ctx = current_context_id();
+    if (ctx == 0 || slot.ctx_id != ctx || slot.addr == nullptr) {
         void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // binds the device's context if none was current
         if (e != cudaSuccess) return e;
-        g_noalloc_addr[dev] = p;
+        slot.addr = p;
+        slot.ctx_id = current_context_id();
     }
-    *out = g_noalloc_addr[dev];
+    *out = slot.addr;
     return cudaSuccess;
 }
 

@@ -31,23 +31,54 @@ def _poisoned(shape):
     return t
 
 
-@pytest.mark.parametrize("B,H,S,D,ragged", [(4, 8, 3000, 128, False), (6, 4, 700, 64, True), (2, 3, 500, 80, False)])
-def test_noalloc_matches_workspace_entry_point_twice(B, H, S, D, ragged):
-    q, K, V, ks, vs = po.random_cache(B * 100 + S, B, H, H, S, D)
+# (B, Hq, Hkv, S, D, ragged, output type): dense MHA on the tensor-core kernel,
+# ragged head_dim 64 on the CUDA-core split kernel, head_dim 80 on the generic
+# kernel, ragged grouped-query heads on the tensor-core kernel (its tile order
+# and split records sit in the shared array), and a bf16 output.
+CASES = [(4, 8, 8, 3000, 128, False, torch.float32), (6, 4, 4, 700, 64, True, torch.float32),
+         (2, 3, 3, 500, 80, False, torch.float32), (3, 16, 2, 1500, 128, True, torch.float32),
+         (3, 16, 2, 2000, 128, False, torch.bfloat16)]
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S,D,ragged,odt", CASES)
+def test_noalloc_matches_workspace_entry_point_twice(B, Hq, Hkv, S, D, ragged, odt):
+    q, K, V, ks, vs = po.random_cache(B * 100 + S, B, Hq, Hkv, S, D)
     lens = np.array([S, 0, 1, 257, S - 1, 128][:B], np.int32) if ragged else None
     tq, tK, tV, tks, tvs = _dev(q, K, V, ks, vs)
     tl = None if lens is None else torch.tensor(lens, device=DEV)
-    ref_out = kvd.decode(tq, tK, tV, tks, tvs, seq_lens=tl)  # existing entry point
+    ref_out = kvd.decode(tq, tK, tV, tks, tvs, seq_lens=tl, out_dtype=odt)  # existing entry point
     torch.cuda.synchronize()
-    ref = ref_out.cpu().numpy()
+    ref = ref_out.float().cpu().numpy()
     f64 = po.decode_f64(q, K, V, ks, vs, seq_lens=lens)
+    rel16 = 2.0 ** -8 if odt == torch.bfloat16 else 0.0  # one bf16 rounding of the output
     for _ in range(2):
-        out = _poisoned((B, H, D))
+        out = torch.empty((B, Hq, D), dtype=odt, device=DEV)
+        out.view(torch.int16 if odt == torch.bfloat16 else torch.int32).fill_(-1)
         kvd.decode_noalloc(tq, tK, tV, tks, tvs, out, seq_lens=tl)
         torch.cuda.synchronize()
-        got = out.cpu().numpy()
+        got = out.float().cpu().numpy()
         assert po.check(got, ref.astype(np.float64), ATOL, RTOL)[0] == 0
-        assert po.check(got, f64, ATOL, RTOL)[0] == 0
+        assert po.check(got, f64, ATOL, RTOL + rel16)[0] == 0
+
+
+def test_noalloc_rejects_long_context_shape():
+    """A dense long-context decode (4 sequences x 32 heads x 131,072 tokens) plans
+    more split records than the fixed array holds: rejected before any launch."""
+    d = kvd.DecodeDesc()
+    d.batch, d.num_q_heads, d.num_kv_heads, d.head_dim, d.max_seq_len = 4, 32, 32, 128, 131072
+    d.kv_stride_h, d.kv_stride_b = 131072 * 128, 32 * 131072 * 128
+    d.sc_stride_h, d.sc_stride_b = 131072, 32 * 131072
+    d.q_stride_h, d.q_stride_b = 128, 32 * 128
+    d.o_stride_h, d.o_stride_b = 128, 32 * 128
+    assert kvd.workspace_size(d) > kvd.NOALLOC_SCRATCH_BYTES
+    dummy = torch.zeros(64, device=DEV)
+    out = torch.full((16,), 7.0, device=DEV)
+    p = dummy.data_ptr()
+    rc = kvd.lib().kvd_decode_launch_noalloc(ctypes.byref(d), p, p, p, p, p, out.data_ptr(),
+                                             torch.cuda.current_stream().cuda_stream)
+    assert rc == kvd.CUDA_ERROR_INVALID_VALUE
+    torch.cuda.synchronize()
+    assert torch.all(out == 7.0)
 
 
 def test_noalloc_rejects_scratch_beyond_its_fixed_size():
