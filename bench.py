@@ -1,22 +1,31 @@
 """Benchmark of the INT8 KV-cache decode-attention path.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config C]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config C] [--only]
 
-One step = one decode of configuration C (default 2: B=64, H=32, D=128,
-S=4096, the Llama-7B-like MHA config the headline metric is quoted on) over
-a KV cache resident in HBM. The cache is 2.2 GB per step, far larger than the
-126 MB L2, so no flush is needed between steps. Multi-GPU (torchrun, one rank
-per GPU): every rank decodes its own batch shard with no communication (weak
-scaling: per-GPU work fixed, global batch = B*N); the step time is the max over
-ranks of CUDA-event time.
+One step = one decode of a BASELINE configuration over a KV cache resident in
+HBM. The headline (`value`) is configuration C (default 2: B=64, H=32, D=128,
+S=4096, the Llama-7B-like MHA config the metric is quoted on); the same line
+also carries every other configuration under `configs` (skipped with --only).
+Caches of configurations 2-5 are 1.1-4.6 GB per step, far larger than the 126 MB
+L2, so no flush is needed between steps; configuration 1 (1.1 MB) is
+launch-latency bound and stays L2-resident, which its entry says.
+
+Multi-GPU (torchrun, one rank per GPU): configurations 1, 2, 4 and 5 shard the
+batch with no communication (weak scaling: every rank decodes a batch of the
+configuration's size); configuration 3 splits the sequence across the ranks
+and merges (m, l, o) records over NVLink (strong scaling: the job is one
+configuration-3 step). Step times are CUDA-event times, max over ranks.
 
 Printed: one JSON line (rank 0). `value` = aggregate algorithmic HBM GB/s;
-`e2e` = the same metric through the reference-facing C ABI call
-(kv_int8_split_launch) with the step's query copied from pinned host memory
-and the output copied back inside the timed region (the cache is decode state
-and stays resident); `roofline` = achieved / measured HBM copy bandwidth;
+`e2e` = the same metric through the reference-facing C ABI call with the
+step's query copied from pinned host memory and the output copied back inside
+the timed region (the cache is decode state and stays resident); `roofline` =
+achieved / measured HBM copy bandwidth; `parity` = a sampled FP64 check of the
+step's output (torch float64 on the device, at least 64 query rows);
 `cpu_baseline` = the reference's fp32 host loop on the host cores for a sample
-of heads. `--impl reference` times that host loop alone as the reference arm.
+of heads; `reference_gpu` = the reference's own four kernels built for sm_100a,
+timed with CUDA events on configurations 1-3 (outside the timed region).
+`--impl reference` times the reference's host loop alone as the reference arm.
 """
 from __future__ import annotations
 
@@ -35,6 +44,8 @@ sys.path.insert(0, str(ROOT / "cuda-operators_b200"))
 
 METRIC = "INT8 KV decode attn: achieved HBM GB/s (% peak), µs/step at 1/2/4/8 GPUs"
 FALLBACK_HBM_GBS = 6650.0
+ATOL, RTOL = 2e-5, 1e-4  # output tolerance of the north-star spec
+CPU_STEPS = 10           # timed host-loop steps in both arms (after one warm-up step)
 
 
 def measured_peak():
@@ -48,7 +59,7 @@ def measured_peak():
 
 
 def committed_traffic(config: int):
-    """DRAM bytes per launch of the split-KV kernel from the committed ncu summary."""
+    """DRAM bytes per launch of the decode kernel from the committed ncu summary."""
     path = ROOT / "profiles" / "traffic.json"
     if not path.exists():
         return None
@@ -145,13 +156,12 @@ def cpu_sample(cfg, heads: int, seed: int):
     return q, K, V, ks, vs, S
 
 
-def cpu_measure(cfg, heads: int, steps: int, seed: int = 17):
+def cpu_measure(cfg, heads: int, steps: int = CPU_STEPS, seed: int = 17) -> dict:
     """Times the reference fp32 host loop (oracle/_ref build when present, else
-    the oracle's restatement) over a sample of heads on all host threads.
-    Returns (GB/s, seconds per step, kind, threads, sample description)."""
+    the oracle's restatement) over a sample of heads on all host threads: one
+    untimed warm-up step, then `steps` timed steps. Returns GB/s of the median
+    step with the min/max spread."""
     import ctypes
-
-    import numpy as np
 
     sys.path.insert(0, str(ROOT / "oracle"))
     import pyoracle as po
@@ -168,21 +178,25 @@ def cpu_measure(cfg, heads: int, steps: int, seed: int = 17):
                                       ks[a:b].ctypes.data, vs[a:b].ctypes.data, b - a, S, D)
                 for a, b in zip(bounds[:-1], bounds[1:])]
         arr = (ctypes.c_void_p * len(jobs))(*jobs)
+        ref.kvref_cpu_run_parallel(arr, len(jobs))  # warm-up: first touch of every job's buffers
         for _ in range(steps):
             times.append(ref.kvref_cpu_run_parallel(arr, len(jobs)))
         for j in jobs:
             ref.kvref_cpu_free(j)
     else:
         kind = "port"
+        po.cpu_reference_f32(q, K, V, ks, vs, heads, S, D, threads)
         for _ in range(steps):
             t0 = time.perf_counter()
             po.cpu_reference_f32(q, K, V, ks, vs, heads, S, D, threads)
             times.append(time.perf_counter() - t0)
-    sec = statistics.median(times)
     nbytes = heads * S * (2 * D + 8) + heads * D * 8
-    sample = (f"{heads} query heads x {S} tokens x D={D} of config {cfg.name} "
-              f"({nbytes / 1e9:.3f} GB/step), median of {steps} steps, {threads} threads")
-    return nbytes / sec / 1e9, sec, kind, threads, sample
+    sec = statistics.median(times)
+    sample = (f"{heads} query heads x {S} tokens x D={D} of config {cfg.name} ({nbytes / 1e9:.3f} GB/step), "
+              f"1 warm-up + median of {steps} steps, {threads} threads")
+    return {"value": nbytes / sec / 1e9, "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample,
+            "ms_per_step": sec * 1e3, "min_gbs": nbytes / max(times) / 1e9, "max_gbs": nbytes / min(times) / 1e9,
+            "steps": steps}
 
 
 def run_reference(args) -> None:
@@ -192,18 +206,90 @@ def run_reference(args) -> None:
     import workload as wl
 
     cfg = wl.CONFIGS[args.config]
-    steps = max(1, min(args.steps, 30))  # bounded: the whole arm stays within a few minutes
-    gbs, sec, kind, threads, sample = cpu_measure(cfg, args.cpu_heads, steps)
+    steps = max(CPU_STEPS, min(args.steps, 30))  # bounded: the whole arm stays within a few minutes
+    cb = cpu_measure(cfg, args.cpu_heads, steps)
     line = {
-        "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
-        "steps": steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": 1, "ms_per_step": cb["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: seeded N(0,1) Q/K/V, K/V quantised per token",
-        "config": {"workload": f"config{args.config} {cfg.name} (host sample)", "sample": sample},
-        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
-        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": {"workload": f"config{args.config} {cfg.name} (host sample)", "sample": cb["sample"]},
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- parity
+def _row_records_f64(case, b: int, hk: int, n: int, scale: float):
+    """FP64 (m, l, o) of the G query heads of item (b, hk) over the first n tokens
+    of this rank's cache (natural-log domain; o unnormalised)."""
+    import torch
+
+    cfg = case.cfg
+    G, D = cfg.group, cfg.head_dim
+    dev = case.q.device
+    if n <= 0:
+        return (torch.full((G,), float("-inf"), dtype=torch.float64, device=dev),
+                torch.zeros(G, dtype=torch.float64, device=dev), torch.zeros(G, D, dtype=torch.float64, device=dev))
+    q = case.q[b, hk * G:(hk + 1) * G].double()
+    k = case.K[b, hk, :n].double() * case.ks[b, hk, :n, None].double()
+    s = (q @ k.T) * scale
+    m = s.max(dim=1).values
+    p = torch.exp(s - m[:, None])
+    v = case.V[b, hk, :n].double() * case.vs[b, hk, :n, None].double()
+    return m, p.sum(dim=1), p @ v
+
+
+def parity_check(case, out, lens, world: int, seqsplit: bool) -> dict:
+    """Compares sampled query rows of `out` with a float64 torch restatement of
+    the decode (score = (q . code) * k_scale / sqrt(D), value = code * v_scale).
+    Sequence split: every rank computes float64 (m, l, o) over its shard and the
+    records are all-gathered and merged. Returns rows checked, bad elements,
+    max abs and max normalised error (max over ranks)."""
+    import math
+
+    import torch
+    import torch.distributed as dist
+
+    import workload as wl
+
+    cfg = case.cfg
+    B = case.q.shape[0]
+    G = cfg.group
+    scale = 1.0 / math.sqrt(cfg.head_dim)
+    items = wl.parity_items(cfg, B, lens)
+    m_l, l_l, o_l = [], [], []
+    for b, hk in items:
+        n = lens[b] if lens is not None else case.K.shape[2]
+        m, l, o = _row_records_f64(case, b, hk, n, scale)
+        m_l.append(m), l_l.append(l), o_l.append(o)
+    M, L, O = torch.stack(m_l), torch.stack(l_l), torch.stack(o_l)  # [items, G], [items, G], [items, G, D]
+    if seqsplit:
+        rec = torch.cat([M[..., None], L[..., None], O], dim=-1).contiguous()
+        allr = [torch.empty_like(rec) for _ in range(world)]
+        dist.all_gather(allr, rec)
+        allr = torch.stack(allr)
+        Mx = allr[..., 0].max(dim=0).values
+        f = torch.where(torch.isfinite(allr[..., 0]), torch.exp(allr[..., 0] - Mx), torch.zeros_like(allr[..., 0]))
+        L = (f * allr[..., 1]).sum(dim=0)
+        O = (f[..., None] * allr[..., 2:]).sum(dim=0)
+    ref = torch.where(L[..., None] > 0, O / L.clamp_min(1e-300)[..., None], torch.zeros_like(O))
+    got = torch.stack([out[b, hk * G:(hk + 1) * G].double() for b, hk in items])
+    err = (got - ref).abs()
+    bad_mask = (err > ATOL + RTOL * ref.abs()) | ~torch.isfinite(got)
+    res = torch.tensor([float(bad_mask.sum().item()), float(err.nan_to_num(float("inf")).max().item()),
+                        float((err / (ATOL + RTOL * ref.abs())).nan_to_num(float("inf")).max().item())],
+                       dtype=torch.float64, device=case.q.device)
+    if world > 1 and not seqsplit:  # every rank checked its own rows: total bad, worst error
+        bad_t = res[:1].clone()
+        dist.all_reduce(bad_t)
+        mx = res[1:].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        res = torch.cat([bad_t, mx])
+    rows = len(items) * G * (world if world > 1 and not seqsplit else 1)
+    return {"rows": rows, "bad": int(res[0].item()), "max_abs": res[1].item(), "max_norm": res[2].item(),
+            "tol": f"|out - f64| <= {ATOL} + {RTOL}|f64|", "ref": "torch float64 on the device"}
 
 
 # ---------------------------------------------------------------- GPU leg
@@ -238,58 +324,103 @@ def to_paged_pool(case, bs: int, Hkv: int, D: int, seed: int, dev):
     return pool
 
 
-def run_ours(args) -> None:
-    import torch
-    import torch.distributed as dist
+class Env:
+    """Process-group facts shared by every measurement."""
 
+    def __init__(self, args):
+        import torch
+        import torch.distributed as dist
+
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device(f"cuda:{self.local}")
+        if self.world > 1:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=self.dev)
+        self.comm = None   # library NCCL communicator (sequence split), made on first use
+        self.args = args
+
+    def library_comm(self):
+        import torch
+        import torch.distributed as dist
+
+        import kvdecode as kvd
+
+        if self.comm is None:
+            uid = torch.zeros(128, dtype=torch.uint8, device=self.dev)
+            if self.rank == 0:
+                uid.copy_(torch.frombuffer(bytearray(kvd.mgpu_unique_id()), dtype=torch.uint8))
+            dist.broadcast(uid, 0)
+            self.comm = kvd.MgpuComm(self.world, self.rank, bytes(uid.cpu().numpy().tobytes()))
+        return self.comm
+
+    def timed(self, fn, n: int, stream) -> float:
+        """Milliseconds per call of fn over n calls: CUDA events on `stream`,
+        barrier + synchronize on both sides, max over ranks."""
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / n
+        if self.world > 1:
+            t = torch.tensor([ms], device=self.dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+
+def measure_config(env: Env, cid: int, steps: int, warmup: int, batch: int = 0, paged: int = 0) -> dict:
+    """Times configuration `cid` on this process group: device steps replayed
+    from CUDA graphs, the end-to-end step through the C ABI with host buffers,
+    then the sampled parity check. Frees the configuration's memory on return."""
+    import dataclasses
+
+    import torch
+
+    import kvd_mgpu as mg
     import kvdecode as kvd
     import workload as wl
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device(f"cuda:{local}")
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
-
-    cfg = wl.CONFIGS[args.config]
-    B = args.batch or cfg.batch
+    args, world, rank, dev = env.args, env.world, env.rank, env.dev
+    cfg = wl.CONFIGS[cid]
+    B = batch or cfg.batch
     # Configuration 3 on N > 1 GPUs splits the sequence: rank g holds tokens
     # [g*S/N, (g+1)*S/N) of every head and the ranks merge (m, l, o) records
-    # over NCCL (strong scaling: the job is one configuration-3 step). The other
-    # configurations shard the batch with no communication (weak scaling).
+    # over NVLink (strong scaling). The others shard the batch (weak scaling).
     seqsplit = cfg.name == "long_context" and world > 1
-    comm = exchange = None
+    exchange = None
     if seqsplit:
-        import dataclasses
-
-        import kvd_mgpu as mg
-
         lo, hi = mg.seq_shard(cfg.seq_len, world, rank, align=128)
         case = wl.make_case(dataclasses.replace(cfg, seq_len=hi - lo), seed=args.seed + rank, device=str(dev),
                             batch=B)
         job_bytes = wl.step_bytes(cfg, batch=B)
         nbytes = kvd.algorithmic_bytes(B, cfg.q_heads, cfg.kv_heads, cfg.head_dim, hi - lo)
         splitter = mg.SeqSplitDecode(B, cfg.q_heads, cfg.head_dim, dev)
-        if args.exchange != "torch":  # a communicator made by the library, its id broadcast by torch
-            uid = torch.zeros(128, dtype=torch.uint8, device=dev)
-            if rank == 0:
-                uid.copy_(torch.frombuffer(bytearray(kvd.mgpu_unique_id()), dtype=torch.uint8))
-            dist.broadcast(uid, 0)
-            comm = kvd.MgpuComm(world, rank, bytes(uid.cpu().numpy().tobytes()))
+        if args.exchange != "torch":
+            comm = env.library_comm()
             if args.exchange == "p2p":
                 exchange = kvd.P2PExchange(comm, B, cfg.q_heads, cfg.head_dim)
     else:
         case = wl.make_case(cfg, seed=args.seed + rank, device=str(dev), batch=B)
     out = torch.empty((B, cfg.q_heads, cfg.head_dim), dtype=torch.float32, device=dev)
     lens0 = case.seq_lens.clone() if cfg.ragged else None
-    lens_final = [n + 1 for n in case.lens_host] if cfg.append else case.lens_host
+    lens_final = [n + 1 for n in case.lens_host] if cfg.append else (case.lens_host if cfg.ragged else None)
     if not seqsplit:
-        nbytes = wl.step_bytes(cfg, lens_final if cfg.ragged else None, batch=B)
+        nbytes = wl.step_bytes(cfg, lens_final, batch=B)
         job_bytes = nbytes * world
-    if args.paged and not seqsplit:
-        pool = to_paged_pool(case, args.paged, cfg.kv_heads, cfg.head_dim, args.seed, dev)
+    if paged and not seqsplit:
+        pool = to_paged_pool(case, paged, cfg.kv_heads, cfg.head_dim, args.seed, dev)
         pdesc = kvd.make_paged_desc(case.q, pool["K"], pool["ks"], out, pool["table"], pool["lens"])
         ws = torch.empty(max(kvd.paged_workspace_size(pdesc), 1), dtype=torch.uint8, device=dev)
     else:
@@ -298,15 +429,17 @@ def run_ours(args) -> None:
         ws = torch.empty(max(kvd.workspace_size(desc), 1), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
     if seqsplit and args.exchange == "nccl":
-        ws_split = torch.empty(int(kvd.lib().kvd_mgpu_seq_split_workspace_size(__import__("ctypes").byref(desc),
-                                                                            world)), dtype=torch.uint8, device=dev)
+        import ctypes
+
+        ws_split = torch.empty(int(kvd.lib().kvd_mgpu_seq_split_workspace_size(ctypes.byref(desc), world)),
+                               dtype=torch.uint8, device=dev)
 
     def step():  # launches on the current stream (a capture stream while a graph is recorded)
         if seqsplit:
             if args.exchange == "p2p":
                 exchange.decode(case.q, case.K, case.V, case.ks, case.vs, out=out)
             elif args.exchange == "nccl":
-                kvd.seq_split_decode(comm, case.q, case.K, case.V, case.ks, case.vs, out=out, workspace=ws_split)
+                kvd.seq_split_decode(env.comm, case.q, case.K, case.V, case.ks, case.vs, out=out, workspace=ws_split)
             else:
                 splitter(case.q, case.K, case.V, case.ks, case.vs, out=out)
             return
@@ -336,7 +469,7 @@ def run_ours(args) -> None:
     else:
         separate = cfg.append and (args.separate_append or pool is not None)
         launches_per_step = kvd.last_launch_count() + (1 if separate else 0)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
 
     # Decode steps are replayed from a CUDA graph (G steps per graph) so that
@@ -344,7 +477,8 @@ def run_ours(args) -> None:
     # sequence split is captured with the peer-store exchange only (its kernel
     # counts epochs on the device); the NCCL and torch exchanges launch eagerly.
     graphable = not seqsplit or args.exchange == "p2p"
-    G = 10 if args.steps % 10 == 0 and not args.no_graph and graphable else 1
+    G = 10 if steps % 10 == 0 and not args.no_graph and graphable else 1
+    graphs = []
     if G > 1:
         graph = torch.cuda.CUDAGraph()
         torch.cuda.synchronize()
@@ -353,31 +487,13 @@ def run_ours(args) -> None:
                 step()
         torch.cuda.synchronize()
         graph.replay()
+        graphs.append(graph)
         run_steps = graph.replay
     else:
         run_steps = step
 
-    def timed(fn, n):
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(n):
-            fn()
-        e1.record(stream)
-        e1.synchronize()
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / n
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
-
-    with ClockSampler(local) as clk:
-        ms = timed(run_steps, args.steps // G) / G
+    with ClockSampler(env.local) as clk:
+        ms = env.timed(run_steps, steps // G, stream) / G
 
     # ---- end to end through the reference-facing C ABI with host buffers
     q_host = case.q.cpu().pin_memory()
@@ -398,12 +514,12 @@ def run_ours(args) -> None:
             step()
         out_host.copy_(out, non_blocking=True)
 
-    for _ in range(max(3, args.warmup // 2)):
+    for _ in range(max(3, warmup // 2)):
         e2e_step()
     # Replayed from a CUDA graph like the device-timed steps (the copies are in the graph),
     # so that host launch overhead does not stand in for the end-to-end time of small configs.
     run_e2e = e2e_step
-    n_e2e = max(10, args.steps // 4)
+    n_e2e = max(10, steps // 4)
     if G > 1 and world == 1:
         e2e_graph = torch.cuda.CUDAGraph()
         torch.cuda.synchronize()
@@ -411,6 +527,7 @@ def run_ours(args) -> None:
             for _ in range(G):
                 e2e_step()
         torch.cuda.synchronize()
+        graphs.append(e2e_graph)
         # the replayed steps must recompute the output: clear it, replay, compare
         expect = out_host.clone()
         out.zero_()
@@ -422,63 +539,184 @@ def run_ours(args) -> None:
         run_e2e = e2e_graph.replay
         n_e2e = max(1, n_e2e // G)
     G_e2e = G if run_e2e is not e2e_step else 1
-    e2e_ms = timed(run_e2e, n_e2e) / G_e2e
+    e2e_ms = env.timed(run_e2e, n_e2e, stream) / G_e2e
+
+    # ---- parity of one more step, outside the timed regions
+    out.view(torch.int32).fill_(-1)
+    step()
+    torch.cuda.synchronize()
+    parity = None
+    if not args.no_parity:
+        if pool is not None:  # the paged pools replaced the dense copy: check against a dense re-decode
+            parity = {"rows": 0, "bad": 0, "note": "paged run: parity is covered by tests/test_paged.py"}
+        else:
+            parity = parity_check(case, out, lens_final, world, seqsplit)
+    status = kvd.device_status()
 
     peak, peak_kind = measured_peak()
     per_gpu_gbs = nbytes / (ms * 1e-3) / 1e9
-    agg_gbs = job_bytes / (ms * 1e-3) / 1e9
-    e2e_gbs = job_bytes / (e2e_ms * 1e-3) / 1e9
-    line = {
-        "metric": METRIC, "value": agg_gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "us_per_step": ms * 1e3,
-        "pct_of_peak": 100.0 * per_gpu_gbs / peak, "higher_is_better": True,
+    res = {
+        "config": cid, "name": cfg.name,
+        "workload": (f"config{cid} {cfg.name}: B={B}/GPU Hq={cfg.q_heads} Hkv={cfg.kv_heads} D={cfg.head_dim} "
+                     f"S={cfg.seq_len}" + (" ragged+append" if cfg.ragged else "")
+                     + (f" paged cache, {paged}-token blocks in random pool order" if pool else "")),
+        "global_batch": B if seqsplit else B * world, "seq_len": cfg.seq_len,
+        "parallelism": (f"sequence split x{world}, (m, l, o) records exchanged "
+                        + ("by peer stores + LSE combine in one kernel" if args.exchange == "p2p"
+                           else "by NCCL all-gather + LSE combine")
+                        if seqsplit else f"batch shards x{world}, no comm"),
         "scaling": "strong" if seqsplit else "weak",
-        "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic: seeded N(0,1) Q/K/V (torch Philox on device), K/V quantised per token by the library",
-        "config": {
-            "workload": (f"config{args.config} {cfg.name}: B={B}/GPU Hq={cfg.q_heads} Hkv={cfg.kv_heads} "
-                         f"D={cfg.head_dim} S={cfg.seq_len}" + (" ragged+append" if cfg.ragged else "")
-                         + (f" paged cache, {args.paged}-token blocks in random pool order" if pool else "")),
-            "global_batch": B if seqsplit else B * world, "seq_len": cfg.seq_len,
-            "parallelism": (f"sequence split x{world}, (m, l, o) records exchanged "
-                            + ("by peer stores + LSE combine in one kernel" if args.exchange == "p2p"
-                               else "by NCCL all-gather + LSE combine")
-                            if seqsplit else f"batch shards x{world}, no comm"),
-            "bytes_per_step_per_gpu": nbytes,
-            "l2": f"no flush: {nbytes / 1e9:.2f} GB of cache read per step > 126 MB L2",
-        },
+        "ms_per_step": ms, "us_per_step": ms * 1e3, "value": job_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
+        "gbs_per_gpu": per_gpu_gbs, "pct_of_peak": 100.0 * per_gpu_gbs / peak,
+        "bytes_per_step_per_gpu": nbytes,
+        "l2": (f"no flush: {nbytes / 1e9:.2f} GB of cache read per step > 126 MB L2" if nbytes > 126e6 else
+               f"L2-resident: {nbytes / 1e6:.2f} MB per step < 126 MB L2 (launch-latency bound, no flush)"),
         "roofline": {"bound": "hbm", "achieved": per_gpu_gbs, "peak": peak, "unit": "GB/s",
                      "frac": per_gpu_gbs / peak, "peak_source": f"{peak_kind} copy bandwidth",
-                     "traffic": committed_traffic(args.config),
-                     "timed": ("decode step: tcgen05 kernel gqa_tc_kernel" if cfg.head_dim == 128
-                               else "decode step: CUDA-core split-KV kernel + boundary combine")
-                              + ((" + record exchange over NVLink peer stores and LSE combine in one kernel"
-                                  if args.exchange == "p2p" else " + NCCL record all-gather + LSE combine")
-                                 if seqsplit else "")
-                              + ((" with the append fused into it" if not (args.separate_append or pool is not None)
-                                  else " after the append kernel") if cfg.append else "")},
+                     "traffic": committed_traffic(cid)},
         "clocks": clk.summary(),
-        "e2e": {"value": e2e_gbs, "unit": "GB/s", "ms_per_step": e2e_ms,
+        "e2e": {"value": job_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
+                "us_per_step": e2e_ms * 1e3,
                 "launch": f"CUDA graph of {G_e2e} steps, copies included" if G_e2e > 1 else "direct launches",
                 "h2d_bytes_per_step": int(q_host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4),
-                "call": ("kv_int8_split_launch" if flat else
-                         "kvd_paged_decode_launch" if pool is not None else "kvd_decode_launch")},
-        "gpu_launches": launches_per_step * args.steps,
-        "launch": f"CUDA graph of {G} steps" if G > 1 else "direct launches",
+                "call": ("kv_int8_split_launch" if flat else "kvd_paged_decode_launch" if pool is not None
+                         else "kvd_mgpu_p2p_seq_split_decode" if seqsplit and args.exchange == "p2p"
+                         else "kvd_mgpu_seq_split_decode" if seqsplit and args.exchange == "nccl"
+                         else "kvd_append_decode_launch" if cfg.append and not args.separate_append
+                         else "kvd_decode_launch")},
+        "parity": parity, "device_status": status,
+        "launches_per_step": launches_per_step, "gpu_launches": launches_per_step * steps,
+        "launch": f"CUDA graph of {G} steps" if G > 1 else "direct launches", "steps": steps,
     }
+    # release everything this configuration holds before the next one is built
+    torch.cuda.synchronize()
+    del graphs
+    if exchange is not None:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()  # no rank unmaps its exchange buffers while a peer could still write them
+        exchange.close()
+    del case, out, ws
+    torch.cuda.empty_cache()
+    return res
+
+
+def reference_gpu(steps: int) -> dict:
+    """The reference's own kernels (kv_cache/*.cu built for sm_100a into
+    oracle/_ref by oracle/Makefile) on configurations 1-3 in their flat [H, S, D]
+    layout: `solve` of KV_int8.cu and KV_int8_single_buffer.cu (default stream),
+    kv_int8_split_launch of KV_int8_split_optimized.cu and kv_int8_simple_launch
+    of new_kvint8.cu (caller scratch, so no allocation is timed). CUDA events
+    around `steps` calls after one warm-up call. Each output is compared with
+    this library's decode of the same inputs (max abs difference)."""
+    import ctypes
+
+    import torch
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import kvdecode as kvd
+    import pyoracle as po
+    import workload as wl
+
+    libs = {name: po.ref_lib(name) for name in ("tiled", "single", "split", "simple")}
+    if any(v is None for v in libs.values()):
+        return {"unavailable": "oracle/_ref was not built (the reference checkout was absent at build time)"}
+    res = {}
+    for cid in (1, 2, 3):
+        cfg = wl.CONFIGS[cid]
+        case = wl.make_case(cfg, seed=17, device="cuda")
+        H, S, D = cfg.batch * cfg.q_heads, cfg.seq_len, cfg.head_dim
+        ours = kvd.decode(case.q, case.K, case.V, case.ks, case.vs)
+        scratch = torch.empty(H * S, dtype=torch.float32, device="cuda")
+        out = torch.empty((H, D), dtype=torch.float32, device="cuda")
+        stream = torch.cuda.current_stream()
+        ptrs = [case.q.data_ptr(), case.K.data_ptr(), case.V.data_ptr(), case.ks.data_ptr(), case.vs.data_ptr(),
+                out.data_ptr()]
+        calls = {
+            "tiled_solve": lambda: libs["tiled"].kvref_tiled_solve(*ptrs, H, S, D),
+            "single_buffer_solve": lambda: libs["single"].kvref_single_solve(*ptrs, H, S, D),
+            "split_launch": lambda: libs["split"].kvref_split_launch(*ptrs, H, S, D, scratch.data_ptr(),
+                                                                    ctypes.c_void_p(stream.cuda_stream)),
+            "simple_launch": lambda: libs["simple"].kvref_simple_launch(*ptrs, H, S, D, scratch.data_ptr(),
+                                                                       ctypes.c_void_p(stream.cuda_stream)),
+        }
+        nbytes = kvd.algorithmic_bytes(cfg.batch, cfg.q_heads, cfg.kv_heads, D, S)
+        row = {}
+        for name, fn in calls.items():
+            out.fill_(float("nan"))
+            fn()
+            torch.cuda.synchronize()
+            diff = (out.view(cfg.batch, cfg.q_heads, D) - ours).abs().max().item()
+            reps = steps if cid < 3 else max(1, steps // 2)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+            e1.synchronize()
+            us = e0.elapsed_time(e1) / reps * 1e3
+            row[name] = {"us_per_step": us, "gbs": nbytes / (us * 1e-6) / 1e9, "max_abs_vs_ours": diff,
+                         "steps": reps}
+        best = min(row, key=lambda k: row[k]["us_per_step"])
+        res[str(cid)] = {"variants": row, "best": best, "best_us_per_step": row[best]["us_per_step"]}
+        del case, scratch, out, ours
+        torch.cuda.empty_cache()
+    res["how"] = "CUDA events, 1 warm-up + 5 calls (config 3: 2), same seeded inputs as this bench"
+    return res
+
+
+def run_ours(args) -> None:
+    import torch
+
+    env = Env(args)
+    world, rank = env.world, env.rank
+    head = measure_config(env, args.config, args.steps, args.warmup, batch=args.batch, paged=args.paged)
+    configs = {}
+    if not args.only:
+        for cid in (1, 2, 3, 4, 5):
+            if cid != args.config:
+                configs[str(cid)] = measure_config(env, cid, args.steps, args.warmup)
+    peak, peak_kind = measured_peak()
+    line = {
+        "metric": METRIC, "value": head["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "us_per_step": head["us_per_step"],
+        "pct_of_peak": head["pct_of_peak"], "higher_is_better": True, "scaling": head["scaling"],
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,1) Q/K/V (torch Philox on device), K/V quantised per token by the library",
+        "config": {"workload": head["workload"], "global_batch": head["global_batch"], "seq_len": head["seq_len"],
+                   "parallelism": head["parallelism"], "bytes_per_step_per_gpu": head["bytes_per_step_per_gpu"],
+                   "l2": head["l2"]},
+        "roofline": dict(head["roofline"], timed=(
+            "decode step: tcgen05 kernel gqa_tc_kernel" if wl_head_dim(args.config) == 128
+            else "decode step: CUDA-core decode kernel")),
+        "clocks": head["clocks"], "e2e": head["e2e"], "parity": head["parity"],
+        "gpu_launches": head["gpu_launches"], "launch": head["launch"],
+    }
+    if configs:
+        line["configs"] = {cid: {k: v for k, v in c.items() if k not in ("steps",)} for cid, c in configs.items()}
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        gbs, sec, kind, threads, sample = cpu_measure(cfg, args.cpu_heads, 3)
-        line["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample}
+        import workload as wl
+
+        line["cpu_baseline"] = cpu_measure(wl.CONFIGS[args.config], args.cpu_heads)
+    if world == 1 and rank == 0 and not args.only and not args.no_reference_gpu:
+        line["reference_gpu"] = reference_gpu(5)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        import torch.distributed as dist
+
         torch.cuda.synchronize()
-        dist.barrier()  # no rank unmaps its exchange buffers while a peer could still write them
-        if exchange is not None:
-            exchange.close()
-        if comm is not None:
-            comm.close()
+        dist.barrier()
+        if env.comm is not None:
+            env.comm.close()
         dist.destroy_process_group()
+
+
+def wl_head_dim(cid: int) -> int:
+    import workload as wl
+
+    return wl.CONFIGS[cid].head_dim
 
 
 def run_prefill(args) -> None:
@@ -526,11 +764,14 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5], help="headline configuration")
+    ap.add_argument("--only", action="store_true", help="measure the headline configuration alone")
     ap.add_argument("--seed", type=int, default=17)
-    ap.add_argument("--batch", type=int, default=0, help="per-GPU batch override (profiling small cases)")
+    ap.add_argument("--batch", type=int, default=0, help="per-GPU batch override (profiling small cases; implies --only)")
     ap.add_argument("--cpu-heads", type=int, default=512, help="query heads in the CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true", help="skip timing the reference's own GPU kernels")
+    ap.add_argument("--no-parity", action="store_true", help="skip the sampled FP64 check after the timed region")
     ap.add_argument("--no-graph", action="store_true", help="launch every step directly instead of from a CUDA graph")
     ap.add_argument("--exchange", choices=["p2p", "nccl", "torch"], default="p2p",
                     help="config 3 on N>1 GPUs: record exchange by peer stores (p2p), the library's NCCL call, "
@@ -538,12 +779,14 @@ def main() -> None:
     ap.add_argument("--separate-append", action="store_true",
                     help="config 4: append kernel then decode (default: one fused append+decode launch)")
     ap.add_argument("--paged", type=int, default=0, metavar="BS",
-                    help="decode through the paged-cache entry point with BS-token blocks (0: dense cache)")
+                    help="decode through the paged-cache entry point with BS-token blocks (0: dense cache; implies --only)")
     ap.add_argument("--prefill", default="", metavar="B,HQ,HKV,L,LQ",
                     help="time the causal prefill kernel on this shape instead (a side measurement)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.batch or args.paged:
+        args.only = True
     if args.prefill:
         run_prefill(args)
     elif args.impl == "reference":

@@ -104,6 +104,30 @@ def make_case(cfg: Config, seed: int = 17, device: str = "cuda", batch: int | No
     return case
 
 
+def parity_items(cfg: Config, batch: int, lens=None, min_rows: int = 64, seed: int = 5) -> list:
+    """(b, kv head) items whose query rows a full-size parity check compares:
+    at least `min_rows` query rows, always the first and last sequence, the last
+    kv head and, for ragged batches, the longest and shortest sequence; the rest
+    drawn from the seed. Each item covers the group's Hq/Hkv query heads."""
+    import numpy as np
+
+    B, Hkv, G = batch, cfg.kv_heads, cfg.group
+    want = max(1, -(-min_rows // G))
+    items = [(0, 0), (B - 1, Hkv - 1), (0, Hkv - 1), (B - 1, 0)]
+    if lens is not None and len(lens):
+        lens = list(lens)
+        items += [(int(np.argmax(lens)), Hkv // 2), (int(np.argmin(lens)), Hkv - 1)]
+    rng = np.random.default_rng(seed)
+    while len(set(items)) < min(want, B * Hkv):
+        items.append((int(rng.integers(B)), int(rng.integers(Hkv))))
+    out, seen = [], set()
+    for it in items:
+        if it not in seen:
+            seen.add(it)
+            out.append(it)
+    return out
+
+
 def step_bytes(cfg: Config, lens=None, batch: int | None = None) -> int:
     """Algorithmic HBM bytes of one decode step (plus append traffic when it runs)."""
     B = cfg.batch if batch is None else batch
