@@ -241,12 +241,25 @@ def _row_records_f64(case, b: int, hk: int, n: int, scale: float):
     return m, p.sum(dim=1), p @ v
 
 
-def parity_check(case, out, lens, world: int, seqsplit: bool) -> dict:
+def rounded_query(q):
+    """The query as the INT8 Q.K mode sees it: each row rounded by the cache's
+    quantiser rule (scale = max|q| / 127, code = clamp(rint(q / scale), -127, 127))."""
+    import torch
+
+    amax = q.abs().amax(dim=-1, keepdim=True)
+    scale = amax / 127.0
+    codes = torch.where(amax > 0, torch.clamp(torch.round(q / scale), -127, 127), torch.zeros_like(q))
+    return codes * scale
+
+
+def parity_check(case, out, lens, world: int, seqsplit: bool, qk_int8: bool = False) -> dict:
     """Compares sampled query rows of `out` with a float64 torch restatement of
     the decode (score = (q . code) * k_scale / sqrt(D), value = code * v_scale).
     Sequence split: every rank computes float64 (m, l, o) over its shard and the
-    records are all-gathered and merged. Returns rows checked, bad elements,
-    max abs and max normalised error (max over ranks)."""
+    records are all-gathered and merged. With `qk_int8` the reference is the
+    exact decode of the per-head rounded query (what that mode computes).
+    Returns rows checked, bad elements, max abs and max normalised error (max
+    over ranks)."""
     import math
 
     import torch
@@ -259,11 +272,15 @@ def parity_check(case, out, lens, world: int, seqsplit: bool) -> dict:
     G = cfg.group
     scale = 1.0 / math.sqrt(cfg.head_dim)
     items = wl.parity_items(cfg, B, lens)
+    q_saved = case.q
+    if qk_int8:
+        case.q = rounded_query(case.q)
     m_l, l_l, o_l = [], [], []
     for b, hk in items:
         n = lens[b] if lens is not None else case.K.shape[2]
         m, l, o = _row_records_f64(case, b, hk, n, scale)
         m_l.append(m), l_l.append(l), o_l.append(o)
+    case.q = q_saved
     M, L, O = torch.stack(m_l), torch.stack(l_l), torch.stack(o_l)  # [items, G], [items, G], [items, G, D]
     if seqsplit:
         rec = torch.cat([M[..., None], L[..., None], O], dim=-1).contiguous()
@@ -289,7 +306,8 @@ def parity_check(case, out, lens, world: int, seqsplit: bool) -> dict:
         res = torch.cat([bad_t, mx])
     rows = len(items) * G * (world if world > 1 and not seqsplit else 1)
     return {"rows": rows, "bad": int(res[0].item()), "max_abs": res[1].item(), "max_norm": res[2].item(),
-            "tol": f"|out - f64| <= {ATOL} + {RTOL}|f64|", "ref": "torch float64 on the device"}
+            "tol": f"|out - f64| <= {ATOL} + {RTOL}|f64|",
+            "ref": "torch float64 on the device" + (", per-head int8-rounded query" if qk_int8 else "")}
 
 
 # ---------------------------------------------------------------- GPU leg
@@ -380,7 +398,8 @@ class Env:
         return ms
 
 
-def measure_config(env: Env, cid: int, steps: int, warmup: int, batch: int = 0, paged: int = 0) -> dict:
+def measure_config(env: Env, cid: int, steps: int, warmup: int, batch: int = 0, paged: int = 0,
+                   qk_int8: bool = False) -> dict:
     """Times configuration `cid` on this process group: device steps replayed
     from CUDA graphs, the end-to-end step through the C ABI with host buffers,
     then the sampled parity check. Frees the configuration's memory on return."""
@@ -455,10 +474,11 @@ def measure_config(env: Env, cid: int, steps: int, warmup: int, batch: int = 0, 
             case.seq_lens.copy_(lens0)  # every step appends at the same positions
             if not args.separate_append:  # quantise-on-append inside the decode launch
                 kvd.append_decode(case.k_new, case.v_new, case.q, case.K, case.V, case.ks, case.vs, case.seq_lens,
-                                  out=out, workspace=ws)
+                                  out=out, workspace=ws, qk_int8=qk_int8)
                 return
             kvd.append(case.k_new, case.v_new, case.K, case.V, case.ks, case.vs, case.seq_lens)
-        kvd.decode(case.q, case.K, case.V, case.ks, case.vs, out=out, seq_lens=case.seq_lens, workspace=ws)
+        kvd.decode(case.q, case.K, case.V, case.ks, case.vs, out=out, seq_lens=case.seq_lens, workspace=ws,
+                   qk_int8=qk_int8)
 
     step()
     if seqsplit and args.exchange == "torch":  # this rank's partial decode, then the record combine
@@ -498,7 +518,7 @@ def measure_config(env: Env, cid: int, steps: int, warmup: int, batch: int = 0, 
     # ---- end to end through the reference-facing C ABI with host buffers
     q_host = case.q.cpu().pin_memory()
     out_host = torch.empty(out.shape, dtype=torch.float32).pin_memory()
-    flat = not cfg.ragged and cfg.q_heads == cfg.kv_heads and not seqsplit and pool is None
+    flat = not cfg.ragged and cfg.q_heads == cfg.kv_heads and not seqsplit and pool is None and not qk_int8
     if flat:
         H = B * cfg.q_heads
         scratch = torch.empty(H * cfg.seq_len, dtype=torch.float32, device=dev)
@@ -550,7 +570,7 @@ def measure_config(env: Env, cid: int, steps: int, warmup: int, batch: int = 0, 
         if pool is not None:  # the paged pools replaced the dense copy: check against a dense re-decode
             parity = {"rows": 0, "bad": 0, "note": "paged run: parity is covered by tests/test_paged.py"}
         else:
-            parity = parity_check(case, out, lens_final, world, seqsplit)
+            parity = parity_check(case, out, lens_final, world, seqsplit, qk_int8)
     status = kvd.device_status()
 
     peak, peak_kind = measured_peak()
@@ -559,6 +579,7 @@ def measure_config(env: Env, cid: int, steps: int, warmup: int, batch: int = 0, 
         "config": cid, "name": cfg.name,
         "workload": (f"config{cid} {cfg.name}: B={B}/GPU Hq={cfg.q_heads} Hkv={cfg.kv_heads} D={cfg.head_dim} "
                      f"S={cfg.seq_len}" + (" ragged+append" if cfg.ragged else "")
+                     + (" INT8 Q.K mode (KVD_FLAG_QK_INT8)" if qk_int8 else "")
                      + (f" paged cache, {paged}-token blocks in random pool order" if pool else "")),
         "global_batch": B if seqsplit else B * world, "seq_len": cfg.seq_len,
         "parallelism": (f"sequence split x{world}, (m, l, o) records exchanged "
@@ -671,12 +692,15 @@ def run_ours(args) -> None:
 
     env = Env(args)
     world, rank = env.world, env.rank
-    head = measure_config(env, args.config, args.steps, args.warmup, batch=args.batch, paged=args.paged)
+    head = measure_config(env, args.config, args.steps, args.warmup, batch=args.batch, paged=args.paged,
+                          qk_int8=args.qk_int8)
     configs = {}
     if not args.only:
         for cid in (1, 2, 3, 4, 5):
             if cid != args.config:
                 configs[str(cid)] = measure_config(env, cid, args.steps, args.warmup)
+        # the INT8 Q.K mode on the grouped-query configuration (a looser, stated tolerance)
+        configs["5_qk_int8"] = measure_config(env, 5, args.steps, args.warmup, qk_int8=True)
     peak, peak_kind = measured_peak()
     line = {
         "metric": METRIC, "value": head["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -766,6 +790,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5], help="headline configuration")
     ap.add_argument("--only", action="store_true", help="measure the headline configuration alone")
+    ap.add_argument("--qk-int8", action="store_true", help="headline in the INT8 Q.K mode (KVD_FLAG_QK_INT8)")
     ap.add_argument("--seed", type=int, default=17)
     ap.add_argument("--batch", type=int, default=0, help="per-GPU batch override (profiling small cases; implies --only)")
     ap.add_argument("--cpu-heads", type=int, default=512, help="query heads in the CPU sample")

@@ -40,7 +40,7 @@ thread_local int tl_launches = 0;
 // Known flags; one Q type, one output type, and typed output only for
 // normalised rows (records are fp32).
 bool flags_ok(uint32_t f) {
-    if ((f & ~(KVD_FLAG_PARTIAL_OUT | kDtypeFlags)) != 0) return false;
+    if ((f & ~(KVD_FLAG_PARTIAL_OUT | KVD_FLAG_QK_INT8 | kDtypeFlags)) != 0) return false;
     if ((f & KVD_FLAG_Q_BF16) && (f & KVD_FLAG_Q_F16)) return false;
     if ((f & KVD_FLAG_OUT_BF16) && (f & KVD_FLAG_OUT_F16)) return false;
     if ((f & KVD_FLAG_PARTIAL_OUT) && (f & (KVD_FLAG_OUT_BF16 | KVD_FLAG_OUT_F16))) return false;
@@ -108,6 +108,12 @@ extern "C" cudaError_t kvd_decode_launch(const kvd_decode_desc* desc, const void
         return cudaErrorInvalidValue;
     if (!workspace) workspace_bytes = 0;
 
+    if (d.flags & KVD_FLAG_QK_INT8) {  // the int8 query mode exists on the tensor-core kernel only
+        if (fast_path_ok(d, Q, K, V) && gqa_path_ok(d))
+            return launch_gqa_tc(d, Q, K, V, k_scale, v_scale, out, workspace, workspace_bytes, stream,
+                                 &tl_launches);
+        return cudaErrorNotSupported;
+    }
     if (!fast_path_ok(d, Q, K, V))
         return launch_generic(d, Q, K, V, k_scale, v_scale, out, workspace, workspace_bytes, stream,
                               &tl_launches);
@@ -255,6 +261,7 @@ extern "C" cudaError_t kvd_paged_decode_launch(const kvd_paged_desc* desc, const
     if (paged_tc_ok(*desc, d, Q, K_pool, V_pool, k_scale_pool, v_scale_pool))
         return launch_gqa_tc(d, Q, K_pool, V_pool, k_scale_pool, v_scale_pool, out, workspace, workspace_bytes,
                              stream, &tl_launches, &pv);
+    if (desc->flags & KVD_FLAG_QK_INT8) return cudaErrorNotSupported;
     return launch_generic(d, Q, K_pool, V_pool, k_scale_pool, v_scale_pool, out, workspace, workspace_bytes, stream,
                           &tl_launches, &pv);
 }
@@ -281,7 +288,7 @@ extern "C" cudaError_t kvd_combine_launch(const float* parts, int num_parts, int
                                           cudaStream_t stream) {
     tl_launches = 0;
     if (!parts || !out || num_parts < 1 || num_heads < 1 || head_dim < 1) return cudaErrorInvalidValue;
-    if (!flags_ok(flags) || (flags & (KVD_FLAG_Q_BF16 | KVD_FLAG_Q_F16))) return cudaErrorInvalidValue;
+    if (!flags_ok(flags) || (flags & (KVD_FLAG_Q_BF16 | KVD_FLAG_Q_F16 | KVD_FLAG_QK_INT8))) return cudaErrorInvalidValue;
     if (part_stride < static_cast<int64_t>(num_heads) * (head_dim + 4) && num_parts > 1) return cudaErrorInvalidValue;
     return launch_combine_parts(parts, num_parts, part_stride, num_heads, head_dim, out, out_stride, flags, stream,
                                 &tl_launches);
@@ -340,7 +347,7 @@ cudaError_t check_prefill(const kvd_prefill_desc* d) {
     if (d->batch < 1 || d->num_q_heads < 1 || d->num_kv_heads < 1 || d->head_dim < 1) return cudaErrorInvalidValue;
     if (d->num_q_heads % d->num_kv_heads != 0 || d->max_seq_len < 1 || d->max_queries < 1)
         return cudaErrorInvalidValue;
-    if (!flags_ok(d->flags) || (d->flags & KVD_FLAG_PARTIAL_OUT)) return cudaErrorInvalidValue;
+    if (!flags_ok(d->flags) || (d->flags & (KVD_FLAG_PARTIAL_OUT | KVD_FLAG_QK_INT8))) return cudaErrorInvalidValue;
     return cudaSuccess;
 }
 }  // namespace

@@ -75,7 +75,7 @@ struct GqaParams {
     int len_add;
 };
 
-template <int G, int NK_, int NV_>
+template <int G, int NK_, int NV_, int QM_>
 struct GqaCfg {
     static constexpr int D = 128;
     static constexpr int TOK = 128;
@@ -86,6 +86,14 @@ struct GqaCfg {
     static constexpr int NWG = G >= 8 ? 2 : 1;                  // epilogue warpgroups, heads split between them
     static constexpr int HPW = G / NWG;                           // heads per warpgroup
     static constexpr int CPW = NP / NWG;                          // MMA columns per warpgroup
+    // Query mode: QM = 0 splits each query row into four exact byte limbs (QK
+    // N = NP, four accumulator columns per head); QM = 1 (KVD_FLAG_QK_INT8)
+    // quantises it to one int8 row per head, so QK has N = 16 and one column
+    // per head: head h of warpgroup w is B row / accumulator column w*QPW + h.
+    static constexpr bool QI8 = QM_ != 0;
+    static constexpr int NQ = QI8 ? 16 : NP;                      // QK MMA N (<= NP)
+    static constexpr int QPW = NQ / NWG;                          // QK rows / columns per warpgroup
+    static constexpr int SW = QI8 ? HPW : CPW;                    // score columns an epilogue thread loads
     static constexpr int THREADS = 32 * (4 * NWG + 2);
     static constexpr int SC_FLOATS = TOK + 4;
     static constexpr int TILE_BYTES = TOK * D;                    // one K or V tile, 128-byte swizzle
@@ -265,10 +273,10 @@ __device__ __forceinline__ void ptile_scales(const GqaParams& p, const PTile& T,
     }
 }
 
-template <int G, int NK, int NV>
+template <int G, int NK, int NV, int QM>
 __device__ __forceinline__ void gqa_producer_paged(const CUtensorMap* kmap, const CUtensorMap* vmap,
                                                    const GqaParams& p, uint8_t* smem) {
-    using C = GqaCfg<G, NK, NV>;
+    using C = GqaCfg<G, NK, NV, QM>;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     GMeta* meta = reinterpret_cast<GMeta*>(smem + C::OFF_META);
     const uint64_t pol = policy_evict_first();
@@ -358,10 +366,10 @@ __device__ __forceinline__ void gqa_producer_paged(const CUtensorMap* kmap, cons
 // Lane 0 streams K tiles, lane 1 streams V tiles with both scale windows and
 // the tile metadata; the two rings are released independently (K as soon as
 // QK has read it, V after PV and the softmax), so K loads run ahead of V.
-template <int G, int NK, int NV>
+template <int G, int NK, int NV, int QM>
 __device__ __forceinline__ void gqa_producer(const CUtensorMap* kmap, const CUtensorMap* vmap, const GqaParams& p,
                                              uint8_t* smem, bool v_side) {
-    using C = GqaCfg<G, NK, NV>;
+    using C = GqaCfg<G, NK, NV, QM>;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     const int R = v_side ? NV : NK;
     uint64_t* full = bars + (v_side ? C::B_VFULL : C::B_KFULL);
@@ -426,9 +434,9 @@ __device__ __forceinline__ void gqa_producer(const CUtensorMap* kmap, const CUte
 }
 
 // ------------------------------------------------------------------ MMA issuer
-template <int G, int NK, int NV>
+template <int G, int NK, int NV, int QM>
 __device__ __forceinline__ bool gqa_mma_pv(uint8_t* smem, uint32_t tmem, int64_t j) {
-    using C = GqaCfg<G, NK, NV>;
+    using C = GqaCfg<G, NK, NV, QM>;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     const int bj = static_cast<int>(j & 1);
     const int sv = static_cast<int>(j % NV);
@@ -451,11 +459,11 @@ __device__ __forceinline__ bool gqa_mma_pv(uint8_t* smem, uint32_t tmem, int64_t
     return true;
 }
 
-template <int G, int NK, int NV>
+template <int G, int NK, int NV, int QM>
 __device__ __forceinline__ void gqa_mma(const GqaParams& p, uint8_t* smem, uint32_t tmem) {
-    using C = GqaCfg<G, NK, NV>;
+    using C = GqaCfg<G, NK, NV, QM>;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-    constexpr uint32_t idesc_qk = idesc_i8(true, true, false, false, C::NP, 128);
+    constexpr uint32_t idesc_qk = idesc_i8(true, true, false, false, C::NQ, 128);
     int64_t i = 0;
     int kq = 0;
     for (int it = next_item(p, blockIdx.x); it < p.n_items; it = next_item(p, it + p.grid), ++kq) {
@@ -477,10 +485,10 @@ __device__ __forceinline__ void gqa_mma(const GqaParams& p, uint8_t* smem, uint3
             }
             mma_commit(&bars[C::B_SFULL + bi]);
             mma_commit(&bars[C::B_KEMPTY + sk]);
-            if (i >= 1 && !gqa_mma_pv<G, NK, NV>(smem, tmem, i - 1)) return;
+            if (i >= 1 && !gqa_mma_pv<G, NK, NV, QM>(smem, tmem, i - 1)) return;
         }
     }
-    if (i >= 1) gqa_mma_pv<G, NK, NV>(smem, tmem, i - 1);
+    if (i >= 1) gqa_mma_pv<G, NK, NV, QM>(smem, tmem, i - 1);
 }
 
 }  // namespace kvd
@@ -490,7 +498,19 @@ namespace kvd {
 // NP consecutive TMEM columns of this warp's lane quarter.
 template <int NP>
 __device__ __forceinline__ void tmem_ld_np(uint32_t taddr, uint32_t (&r)[NP]) {
-    if constexpr (NP == 16) {
+    if constexpr (NP == 1) {
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r[0]) : "r"(taddr));
+    } else if constexpr (NP == 2) {
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(taddr));
+    } else if constexpr (NP == 4) {
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(taddr));
+    } else if constexpr (NP == 8) {
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                       "=r"(r[7])
+                     : "r"(taddr));
+    } else if constexpr (NP == 16) {
         tmem_ld16(taddr, r);
     } else if constexpr (NP == 32) {
         tmem_ld32(taddr, r);
@@ -572,10 +592,10 @@ __device__ __forceinline__ bool epi_reduce(float (&v)[K], float* red, uint64_t* 
 // four signed bytes written into the K-major 128-byte-swizzled B operand
 // (row 4h + j). Every thread of the warpgroup ends with the same reduced
 // maxima, so each keeps the per-head scales 2^-E_h (sEn) in registers.
-template <int G, int NK, int NV>
+template <int G, int NK, int NV, int QM>
 __device__ __forceinline__ bool gqa_qlimbs(const GqaParams& p, uint8_t* smem, int it, int buf, uint32_t& use,
-                                           float (&sEn)[GqaCfg<G, NK, NV>::HPW]) {
-    using C = GqaCfg<G, NK, NV>;
+                                           float (&sEn)[GqaCfg<G, NK, NV, QM>::HPW]) {
+    using C = GqaCfg<G, NK, NV, QM>;
     constexpr int HPW = C::HPW;
     const int wg = threadIdx.x >> 7, r = threadIdx.x & 127, lane = threadIdx.x & 31;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -588,13 +608,29 @@ __device__ __forceinline__ bool gqa_qlimbs(const GqaParams& p, uint8_t* smem, in
     float qv[HPW], am[HPW];
 #pragma unroll
     for (int h = 0; h < HPW; ++h) {
-        qv[h] = load_q(p.Q, q0 + h * p.q_sh, p.flags) * p.qscale;
+        const float x = load_q(p.Q, q0 + h * p.q_sh, p.flags);
+        qv[h] = C::QI8 ? x : x * p.qscale;  // the int8 query is the raw row, quantised like a cache row
         am[h] = fabsf(qv[h]);
     }
     if (!epi_reduce<HPW, true>(am, red, red_bar, use)) return false;
     uint8_t* qb = smem + C::OFF_QB + buf * C::QB_BYTES;
 #pragma unroll
     for (int h = 0; h < HPW; ++h) {
+        if constexpr (C::QI8) {
+            // The cache's quantiser rule (kvd_quant.cuh): scale = max|q| / 127 and
+            // code = clamp(rint(q / scale), -127, 127), both IEEE; a zero row gives
+            // scale 0 and codes 0. One B row per head: row wg*QPW + h.
+            float sq = 0.f, c = 0.f;
+            if (am[h] != 0.f) {
+                sq = am[h] / 127.0f;
+                c = fminf(fmaxf(rintf(qv[h] / sq), -127.0f), 127.0f);
+            }
+            const int n = wg * C::QPW + h;
+            qb[(n >> 3) * 1024 + (n & 7) * 128 + ((((r >> 4) ^ (n & 7)) << 4) | (r & 15))] =
+                static_cast<uint8_t>(static_cast<int8_t>(c));
+            sEn[h] = sq * p.qscale;
+            continue;
+        }
         const int E = am[h] > 0.f ? min(126, max(-126, 30 - exp_above(am[h]))) : 0;  // |q| * 2^E < 2^30
         int qi = __float2int_rn(qv[h] * pow2i(E));
 #pragma unroll
@@ -622,9 +658,9 @@ __device__ __forceinline__ bool gqa_qlimbs(const GqaParams& p, uint8_t* smem, in
 // (one float4 per lane, the rule and bits of quantize_row_warp), makes the
 // writes visible to the TMA engine and arrives on the append barrier, which
 // the producer waits on before the first tile holding a new token.
-template <int G, int NK, int NV>
+template <int G, int NK, int NV, int QM>
 __device__ __forceinline__ void fused_append_rows(const GqaParams& p, uint8_t* smem) {
-    using C = GqaCfg<G, NK, NV>;
+    using C = GqaCfg<G, NK, NV, QM>;
     constexpr int ET = 128 * C::NWG;  // epilogue threads
     constexpr int EW = ET / 32;
     const int t = threadIdx.x, lane = t & 31, w = t >> 5;
@@ -684,13 +720,13 @@ struct PvSnap {
 };
 
 // PV epilogue of tile A.i for this warpgroup's heads (thread r = output dim r).
-template <int G, int NK, int NV>
+template <int G, int NK, int NV, int QM>
 __device__ __forceinline__ bool gqa_pv_epi(const GqaParams& p, uint8_t* smem, uint32_t tmem, const PvSnap& A,
-                                           const float (&mA)[GqaCfg<G, NK, NV>::HPW],
-                                           const int (&FA)[GqaCfg<G, NK, NV>::HPW],
-                                           const float (&LA)[GqaCfg<G, NK, NV>::HPW],
-                                           float (&o)[GqaCfg<G, NK, NV>::HPW], float (&mpv)[GqaCfg<G, NK, NV>::HPW]) {
-    using C = GqaCfg<G, NK, NV>;
+                                           const float (&mA)[GqaCfg<G, NK, NV, QM>::HPW],
+                                           const int (&FA)[GqaCfg<G, NK, NV, QM>::HPW],
+                                           const float (&LA)[GqaCfg<G, NK, NV, QM>::HPW],
+                                           float (&o)[GqaCfg<G, NK, NV, QM>::HPW], float (&mpv)[GqaCfg<G, NK, NV, QM>::HPW]) {
+    using C = GqaCfg<G, NK, NV, QM>;
     constexpr int NP = C::NP, HPW = C::HPW, CPW = C::CPW;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     uint64_t* o_full = bars + C::B_OFULL;
@@ -742,9 +778,9 @@ __device__ __forceinline__ bool gqa_pv_epi(const GqaParams& p, uint8_t* smem, ui
 
 // One epilogue warpgroup: scores, online softmax and weight limbs of every
 // tile for heads [wg*HPW, (wg+1)*HPW), then the PV epilogue one tile behind.
-template <int G, int NK, int NV>
+template <int G, int NK, int NV, int QM>
 __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, uint32_t tmem) {
-    using C = GqaCfg<G, NK, NV>;
+    using C = GqaCfg<G, NK, NV, QM>;
     constexpr int NP = C::NP, HPW = C::HPW, CPW = C::CPW;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     uint64_t* vfull = bars + C::B_VFULL;
@@ -756,15 +792,15 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
     uint64_t* red_bar = bars + C::B_RED + wg;
     float* red = reinterpret_cast<float*>(smem + C::OFF_RED) + wg * 256;
     const GMeta* meta = reinterpret_cast<const GMeta*>(smem + C::OFF_META);
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16) + wg * CPW;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16) + wg * C::QPW;  // this warpgroup's scores
     uint32_t use = 0;
 
-    if (p.k_new) fused_append_rows<G, NK, NV>(p, smem);
+    if (p.k_new) fused_append_rows<G, NK, NV, QM>(p, smem);
 
     // Zero this warpgroup's rows of both query-limb buffers (pad rows stay
     // zero), then item 0's limbs (its reduction orders the zeroing first).
     {
-        const int rows = NP / C::NWG;
+        const int rows = C::NQ / C::NWG;
         for (int x = r; x < 2 * rows * 8; x += 128) {
             const int buf = x / (rows * 8), rem = x % (rows * 8);
             const int n = wg * rows + rem / 8, chunk = rem % 8;
@@ -773,7 +809,7 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
         }
     }
     float sEn[HPW];
-    if (!gqa_qlimbs<G, NK, NV>(p, smem, next_item(p, blockIdx.x), 0, use, sEn)) return;
+    if (!gqa_qlimbs<G, NK, NV, QM>(p, smem, next_item(p, blockIdx.x), 0, use, sEn)) return;
 
     float m[HPW], l[HPW], sE[HPW], o[HPW], mpv[HPW], mA[HPW], LA[HPW];
     int FA[HPW];
@@ -792,8 +828,8 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
             // ---- scores of tile i (thread r = token r of the tile)
             if (!mbar_wait(&s_full[bi], static_cast<uint32_t>((i >> 1) & 1))) return;
             tc_fence_after();
-            uint32_t sr[CPW];
-            tmem_ld_np<CPW>(lane_base + bi * NP, sr);
+            uint32_t sr[C::SW];
+            tmem_ld_np<C::SW>(lane_base + bi * NP, sr);
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
@@ -815,7 +851,10 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
             float sc[HPW], rv[HPW + 1];
 #pragma unroll
             for (int h = 0; h < HPW; ++h) {
-                const float dot = combine_limbs(sr[4 * h], sr[4 * h + 1], sr[4 * h + 2], sr[4 * h + 3]);
+                // int8 query: one exact int32 column (|acc| <= 128*127*127 < 2^24) per head
+                float dot;
+                if constexpr (C::QI8) dot = __int2float_rn(static_cast<int>(sr[h]));
+                else dot = combine_limbs(sr[4 * h], sr[4 * h + 1], sr[4 * h + 2], sr[4 * h + 3]);
                 sc[h] = valid ? dot * sE[h] * ksv : -INFINITY;
                 rv[h] = sc[h];
             }
@@ -824,7 +863,7 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
             // (thread r = output dim r) while the other warps catch up, then
             // collect the warpgroup maxima.
             epi_reduce_post<HPW + 1, true>(rv, red, red_bar, use);
-            if (A.i >= 0 && !gqa_pv_epi<G, NK, NV>(p, smem, tmem, A, mA, FA, LA, o, mpv)) return;
+            if (A.i >= 0 && !gqa_pv_epi<G, NK, NV, QM>(p, smem, tmem, A, mA, FA, LA, o, mpv)) return;
             if (!epi_reduce_finish<HPW + 1, true>(rv, red, red_bar, use)) return;
             const float vsmax = rv[HPW];
             // ---- online softmax (base 2, lazy max) and the weight limbs
@@ -870,7 +909,7 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
             }
             if (tt == 0) {
                 const int nxt = next_item(p, it + p.grid);
-                if (nxt < p.n_items && !gqa_qlimbs<G, NK, NV>(p, smem, nxt, (kq + 1) & 1, use, sEn)) return;
+                if (nxt < p.n_items && !gqa_qlimbs<G, NK, NV, QM>(p, smem, nxt, (kq + 1) & 1, use, sEn)) return;
             }
 #pragma unroll
             for (int h = 0; h < HPW; ++h) { mA[h] = m[h]; FA[h] = FB[h]; LA[h] = LB[h]; }
@@ -879,7 +918,7 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
             A.flags = mt.flags;
         }
     }
-    if (A.i >= 0) gqa_pv_epi<G, NK, NV>(p, smem, tmem, A, mA, FA, LA, o, mpv);
+    if (A.i >= 0) gqa_pv_epi<G, NK, NV, QM>(p, smem, tmem, A, mA, FA, LA, o, mpv);
 }
 
 // Fused append, end of a CTA: once every thread of the CTA is past its last
@@ -903,10 +942,10 @@ __device__ __forceinline__ void fused_append_finish(const GqaParams& p) {
     }
 }
 
-template <int G, int NK, int NV, int MINB>
-__global__ void __launch_bounds__(GqaCfg<G, NK, NV>::THREADS, MINB) gqa_tc_kernel(
+template <int G, int NK, int NV, int QM, int MINB>
+__global__ void __launch_bounds__(GqaCfg<G, NK, NV, QM>::THREADS, MINB) gqa_tc_kernel(
     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const GqaParams p) {
-    using C = GqaCfg<G, NK, NV>;
+    using C = GqaCfg<G, NK, NV, QM>;
     constexpr int EW = 4 * C::NWG;  // epilogue warps; then the producer warp, then the MMA warp
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -947,11 +986,11 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV>::THREADS, MINB) gqa_tc_kerne
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + C::OFF_TMEM);
     if (warp == EW) {
-        if (p.table) gqa_producer_paged<G, NK, NV>(&kmap, &vmap, p, smem);
-        else if (lane < 2) gqa_producer<G, NK, NV>(&kmap, &vmap, p, smem, lane == 1);
+        if (p.table) gqa_producer_paged<G, NK, NV, QM>(&kmap, &vmap, p, smem);
+        else if (lane < 2) gqa_producer<G, NK, NV, QM>(&kmap, &vmap, p, smem, lane == 1);
     } else if (warp == EW + 1) {
         if (lane == 0) {
-            gqa_mma<G, NK, NV>(p, smem, tmem);
+            gqa_mma<G, NK, NV, QM>(p, smem, tmem);
             mma_commit(drain);  // arrives once every MMA issued above has completed
             mbar_wait(drain, 0);
             mbar_wait(done, 0);  // epilogue warps have finished reading TMEM
@@ -960,7 +999,7 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV>::THREADS, MINB) gqa_tc_kerne
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
     } else {
-        gqa_epilogue<G, NK, NV>(p, smem, tmem);
+        gqa_epilogue<G, NK, NV, QM>(p, smem, tmem);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(done);
@@ -1130,10 +1169,10 @@ int gqa_split_count(const kvd_decode_desc& d) {
     return best_p;
 }
 
-template <int G>
+template <int G, int QM>
 cudaError_t launch_gqa_g(const CUtensorMap& km, const CUtensorMap& vm, const GqaParams& p, cudaStream_t st) {
-    using C = GqaCfg<G, kGqaNK, kGqaNV>;
-    auto kern = gqa_tc_kernel<G, kGqaNK, kGqaNV, kGqaCtas>;
+    using C = GqaCfg<G, kGqaNK, kGqaNV, QM>;
+    auto kern = gqa_tc_kernel<G, kGqaNK, kGqaNV, QM, kGqaCtas>;
     static PerDeviceOnce once;
     const cudaError_t e = once.run([kern] {
         return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
@@ -1261,12 +1300,13 @@ cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const void* Q, const int8_t*
         if (e != cudaSuccess) return e;
         ++*launches;
     }
+    const bool qi8 = (d.flags & KVD_FLAG_QK_INT8) != 0;
     switch (G) {
-        case 1: e = launch_gqa_g<1>(km, vm, p, st); break;
-        case 2: e = launch_gqa_g<2>(km, vm, p, st); break;
-        case 4: e = launch_gqa_g<4>(km, vm, p, st); break;
-        case 8: e = launch_gqa_g<8>(km, vm, p, st); break;
-        case 16: e = launch_gqa_g<16>(km, vm, p, st); break;
+        case 1: e = qi8 ? launch_gqa_g<1, 1>(km, vm, p, st) : launch_gqa_g<1, 0>(km, vm, p, st); break;
+        case 2: e = qi8 ? launch_gqa_g<2, 1>(km, vm, p, st) : launch_gqa_g<2, 0>(km, vm, p, st); break;
+        case 4: e = qi8 ? launch_gqa_g<4, 1>(km, vm, p, st) : launch_gqa_g<4, 0>(km, vm, p, st); break;
+        case 8: e = qi8 ? launch_gqa_g<8, 1>(km, vm, p, st) : launch_gqa_g<8, 0>(km, vm, p, st); break;
+        case 16: e = qi8 ? launch_gqa_g<16, 1>(km, vm, p, st) : launch_gqa_g<16, 0>(km, vm, p, st); break;
         default: return cudaErrorInvalidValue;
     }
     if (e != cudaSuccess) return e;

@@ -51,7 +51,7 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // The local decode's descriptor: same shard, partial records into the workspace.
 kvd_decode_desc record_desc(const kvd_decode_desc& d) {
     kvd_decode_desc r = d;
-    r.flags = KVD_FLAG_PARTIAL_OUT | (d.flags & (KVD_FLAG_Q_BF16 | KVD_FLAG_Q_F16));
+    r.flags = KVD_FLAG_PARTIAL_OUT | (d.flags & (KVD_FLAG_Q_BF16 | KVD_FLAG_Q_F16 | KVD_FLAG_QK_INT8));
     r.o_stride_h = d.head_dim + 4;
     r.o_stride_b = static_cast<int64_t>(d.num_q_heads) * r.o_stride_h;
     return r;

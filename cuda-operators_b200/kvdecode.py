@@ -28,6 +28,7 @@ KVD_FLAG_Q_BF16 = 2
 KVD_FLAG_Q_F16 = 4
 KVD_FLAG_OUT_BF16 = 8
 KVD_FLAG_OUT_F16 = 16
+KVD_FLAG_QK_INT8 = 32
 KVD_STATUS_OK = 0
 KVD_STATUS_WAIT_TIMEOUT = 1
 KVD_STATUS_CACHE_FULL = 2
@@ -281,8 +282,10 @@ def dtype_flags(q=None, out=None, partial: bool = False) -> int:
 
 
 def make_desc(q, k, ks, out, seq_lens=None, max_seq_len: int | None = None, softmax_scale: float = 0.0,
-              partial: bool = False) -> DecodeDesc:
-    """Descriptor for q [B,Hq,D], k/v [B,Hkv,cap,D] int8, ks/vs [B,Hkv,cap], out [B,Hq,D or D+4]."""
+              partial: bool = False, qk_int8: bool = False) -> DecodeDesc:
+    """Descriptor for q [B,Hq,D], k/v [B,Hkv,cap,D] int8, ks/vs [B,Hkv,cap], out [B,Hq,D or D+4].
+    ``qk_int8`` selects the INT8 Q.K mode (KVD_FLAG_QK_INT8: the query is rounded per head
+    to int8 by the cache's quantiser rule)."""
     B, Hq, D = q.shape
     Bk, Hkv, cap, Dk = k.shape
     if Bk != B or Dk != D or Hq % Hkv:
@@ -292,7 +295,7 @@ def make_desc(q, k, ks, out, seq_lens=None, max_seq_len: int | None = None, soft
     d = DecodeDesc()
     d.batch, d.num_q_heads, d.num_kv_heads, d.head_dim = B, Hq, Hkv, D
     d.max_seq_len = cap if max_seq_len is None else max_seq_len
-    d.flags = dtype_flags(q, out, partial)
+    d.flags = dtype_flags(q, out, partial) | (KVD_FLAG_QK_INT8 if qk_int8 else 0)
     d.seq_lens = _ptr(seq_lens)
     d.kv_stride_b, d.kv_stride_h = k.stride(0), k.stride(1)
     d.sc_stride_b, d.sc_stride_h = ks.stride(0), ks.stride(1)
@@ -307,10 +310,10 @@ def workspace_size(desc: DecodeDesc) -> int:
 
 
 def decode(q, k, v, ks, vs, out=None, seq_lens=None, softmax_scale: float = 0.0, partial: bool = False,
-           workspace=None, max_seq_len: int | None = None, stream=None, out_dtype=None):
+           workspace=None, max_seq_len: int | None = None, stream=None, out_dtype=None, qk_int8: bool = False):
     """Split-KV INT8 decode attention; returns ``out`` ([B,Hq,D], or [B,Hq,D+4] records if partial).
     ``q`` may be float32, bfloat16 or float16; the output type is ``out``'s (or ``out_dtype``,
-    default float32)."""
+    default float32). ``qk_int8`` selects the INT8 Q.K mode (looser, stated tolerance)."""
     import torch
 
     B, Hq, D = q.shape
@@ -318,7 +321,7 @@ def decode(q, k, v, ks, vs, out=None, seq_lens=None, softmax_scale: float = 0.0,
         out = torch.empty((B, Hq, D + 4 if partial else D), dtype=out_dtype or torch.float32, device=q.device)
     if v.stride() != k.stride() or vs.stride() != ks.stride():
         raise ValueError("K/V and k_scale/v_scale must share strides")
-    desc = make_desc(q, k, ks, out, seq_lens, max_seq_len, softmax_scale, partial)
+    desc = make_desc(q, k, ks, out, seq_lens, max_seq_len, softmax_scale, partial, qk_int8)
     if workspace is None:
         n = workspace_size(desc)
         workspace = torch.empty(max(n, 1), dtype=torch.uint8, device=q.device)
@@ -373,7 +376,7 @@ def append(k_new, v_new, K, V, ks, vs, seq_lens, stream=None) -> None:
 
 
 def append_decode(k_new, v_new, q, k, v, ks, vs, seq_lens, out=None, workspace=None, softmax_scale: float = 0.0,
-                  partial: bool = False, stream=None, out_dtype=None):
+                  partial: bool = False, stream=None, out_dtype=None, qk_int8: bool = False):
     """Quantise-on-append of one token per (b, kv head) and the decode over the grown
     cache in one decode launch (``kvd_append_decode_launch``); ``seq_lens`` is updated."""
     import torch
@@ -383,7 +386,7 @@ def append_decode(k_new, v_new, q, k, v, ks, vs, seq_lens, out=None, workspace=N
         out = torch.empty((B, Hq, D + 4 if partial else D), dtype=out_dtype or torch.float32, device=q.device)
     if v.stride() != k.stride() or vs.stride() != ks.stride() or v_new.stride() != k_new.stride():
         raise ValueError("K/V (and their scales, and the new rows) must share strides")
-    desc = make_desc(q, k, ks, out, seq_lens, None, softmax_scale, partial)
+    desc = make_desc(q, k, ks, out, seq_lens, None, softmax_scale, partial, qk_int8)
     if workspace is None:
         workspace = torch.empty(max(workspace_size(desc), 1), dtype=torch.uint8, device=q.device)
     rc = lib().kvd_append_decode_launch(ctypes.byref(desc), _ptr(k_new), _ptr(v_new), k_new.stride(0),

@@ -75,6 +75,20 @@ cudaError_t kv_int8_simple_launch(const float* Q, const int8_t* K_int8, const in
  * nearest even). Not combinable with KVD_FLAG_PARTIAL_OUT: records are fp32. */
 #define KVD_FLAG_OUT_BF16 8u
 #define KVD_FLAG_OUT_F16 16u
+/* INT8 Q.K fast mode (no reference counterpart; the reference computes Q.K in
+ * fp32 over dequantised codes, kv_cache/KV_int8_split_optimized.cu:136-143).
+ * Each query row (b, hq) is first quantised with the cache's own rule
+ * (scale_q = max|q|/127, code = clamp(rint(q/scale_q), -127, 127), IEEE fp32)
+ * and Q.K runs as one exact int8 tensor-core product per head:
+ * score = (sum_d code_q * code_k) * scale_q * k_scale * softmax_scale. The
+ * result equals the exact decode of the rounded query q^ = code_q * scale_q
+ * within the usual tolerance (2e-5 + 1e-4 |ref|); against the unrounded query
+ * it carries the rounding's effect, to first order at most
+ * 2 * max_t |ds_t| * max_t |v_t| per output element, where ds_t is the score
+ * change (q^ - q) . k_t * softmax_scale (the looser, stated tolerance of this
+ * mode). Tensor-core kernel only: head_dim 128, groups 1/2/4/8/16, 16-byte
+ * aligned Q/K/V; other shapes return cudaErrorNotSupported. */
+#define KVD_FLAG_QK_INT8 32u
 
 /* A partial record (KVD_FLAG_PARTIAL_OUT output and kvd_combine_launch input)
  * is KVD_PARTIAL_STRIDE(D) floats: [0] = m, a reference point in base-2
