@@ -438,6 +438,12 @@ def measure_config(env: Env, cid: int, steps: int, warmup: int, batch: int = 0, 
     if not seqsplit:
         nbytes = wl.step_bytes(cfg, lens_final, batch=B)
         job_bytes = nbytes * world
+        if world > 1 and cfg.ragged:  # every rank draws its own lengths: add up the ranks' bytes
+            import torch.distributed as dist
+
+            t = torch.tensor([float(nbytes)], dtype=torch.float64, device=dev)
+            dist.all_reduce(t)
+            job_bytes = int(t.item())
     if paged and not seqsplit:
         pool = to_paged_pool(case, paged, cfg.kv_heads, cfg.head_dim, args.seed, dev)
         pdesc = kvd.make_paged_desc(case.q, pool["K"], pool["ks"], out, pool["table"], pool["lens"])
@@ -574,7 +580,8 @@ def measure_config(env: Env, cid: int, steps: int, warmup: int, batch: int = 0, 
     status = kvd.device_status()
 
     peak, peak_kind = measured_peak()
-    per_gpu_gbs = nbytes / (ms * 1e-3) / 1e9
+    # per GPU: the job's bytes over the ranks (a sequence split divides one step's bytes)
+    per_gpu_gbs = job_bytes / world / (ms * 1e-3) / 1e9
     res = {
         "config": cid, "name": cfg.name,
         "workload": (f"config{cid} {cfg.name}: B={B}/GPU Hq={cfg.q_heads} Hkv={cfg.kv_heads} D={cfg.head_dim} "

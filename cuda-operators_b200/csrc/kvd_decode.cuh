@@ -162,10 +162,17 @@ cudaError_t launch_combine_records(const float* base, int nparts, int64_t part_s
                                    uint32_t flags, cudaStream_t st, int* launches);
 bool gqa_path_ok(const kvd_decode_desc& d);
 size_t gqa_workspace_size(const kvd_decode_desc& d);
+// Split records a dense tensor-core decode left in its workspace when the
+// caller asked it to skip the combine: row r's P records of D+4 floats start
+// at partials + r*P*(D+4). P == 1: the rows were written to `out` directly.
+struct SplitRecords {
+    const float* partials;
+    int P;
+};
 cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const void* Q, const int8_t* K, const int8_t* V,
                           const float* ks, const float* vs, void* out, void* ws, size_t ws_bytes,
                           cudaStream_t st, int* launches, const PagedView* pv = nullptr,
-                          const AppendView* av = nullptr);
+                          const AppendView* av = nullptr, SplitRecords* keep_splits = nullptr);
 bool gqa_fused_append_ok(const kvd_decode_desc& d, size_t ws_bytes);
 // 4-D TMA view {D bytes, tokens, kv heads, batch} of a dense K or V cache with
 // a box of 128 bytes x `rows` tokens, 128-byte swizzle (CUtensorMap* as void*).

@@ -1242,7 +1242,8 @@ size_t gqa_workspace_size(const kvd_decode_desc& d) {
 
 cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const void* Q, const int8_t* K, const int8_t* V,
                           const float* ks, const float* vs, void* out, void* ws, size_t ws_bytes,
-                          cudaStream_t st, int* launches, const PagedView* pv, const AppendView* av) {
+                          cudaStream_t st, int* launches, const PagedView* pv, const AppendView* av,
+                          SplitRecords* keep_splits) {
     const int G = d.num_q_heads / d.num_kv_heads;
     const GqaPlan g = plan_gqa(d, ws ? ws_bytes : 0);
     const int S = d.max_seq_len;
@@ -1311,6 +1312,11 @@ cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const void* Q, const int8_t*
     }
     if (e != cudaSuccess) return e;
     ++*launches;
+    if (keep_splits) {  // the caller merges the split records itself (dense batches only)
+        keep_splits->partials = g.P > 1 && !d.seq_lens ? p.partials : nullptr;
+        keep_splits->P = g.P > 1 && !d.seq_lens ? g.P : 1;
+        if (g.P == 1 || !d.seq_lens) return cudaSuccess;
+    }
     if (g.P > 1) {
         const int64_t rows = static_cast<int64_t>(d.batch) * d.num_q_heads;
         if (d.seq_lens) {

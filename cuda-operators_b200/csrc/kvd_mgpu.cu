@@ -142,21 +142,31 @@ extern "C" cudaError_t kvd_mgpu_seq_split_decode(const kvd_decode_desc* desc, co
 
 // ---------------------------------------------------------------- peer exchange
 // The sequence split without NCCL on the hot path: after the local decode, ONE
-// kernel pushes this rank's records straight into every rank's gather buffer
-// over NVLink (peer stores through CUDA IPC mappings), raises a flag per (rank,
-// CTA) in every peer's memory, waits (bounded) for all ranks' flags of its own
-// rows and merges them. NCCL is used once, at set-up, to swap the IPC handles.
+// kernel merges this rank's split records of each row, pushes the merged
+// record straight into every rank's gather buffer over NVLink (peer stores
+// through CUDA IPC mappings), raises a flag per (rank, CTA) in every peer's
+// memory, waits (bounded) for all ranks' flags and merges the gathered records
+// into output rows. NCCL is used at set-up (to swap the IPC handles) and by
+// the collective reset only.
+//
+// Persistent grid: the kernel runs at most as many CTAs as fit on the GPU at
+// once, each looping over row blocks (first pushing all of them, then waiting).
+// Every CTA therefore runs and pushes before any CTA of this rank has to wait,
+// so no CTA waits on a peer CTA that cannot be scheduled, whatever the batch.
 //
 // Epochs: CTA c keeps its own call count in local device memory; every rank
 // runs the same calls, so CTA c of every rank uses the same epoch e and writes
 // buffer parity e & 1. A rank can be at most one epoch ahead of a peer (its
-// step e + 1 waited for the peer's step e flags... which the peer raised after
-// finishing step e - 1), so two parities never collide.
+// step e + 1 needs the peer's step-e flags, raised after the peer finished
+// step e - 1), so two parities never collide. A rank that misses a call breaks
+// that agreement: the others time out, and kvd_mgpu_p2p_reset restores it.
 namespace kvd {
 namespace {
 
-constexpr int kP2PRows = 4;         // record rows per CTA of the exchange kernel
+constexpr int kP2PRows = 1;         // record rows per block of the exchange kernel
+constexpr int kP2PThreads = 128;
 constexpr int kMaxRanks = 8;
+constexpr int kMaxMerge = 256;      // records merged per row (split count cap of the planner)
 
 struct P2PPeers {
     float* gather[kMaxRanks];        // rank p's gather buffer [2][nranks][rows][D+4]
@@ -173,26 +183,91 @@ __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
     return v;
 }
 
-__global__ void __launch_bounds__(128) p2p_exchange_combine_kernel(
-    const float* __restrict__ local, const P2PPeers peers, unsigned int* epochs, int nranks, int rank, int rows,
-    int D, int rows_per_b, void* out, int64_t o_sb, int64_t o_sh, uint32_t flags) {
+// Log-sum-exp weights of the n records of one row (record k at first +
+// k*stride, n <= kMaxMerge), computed by the whole CTA: the records' maxima
+// and weights wk[k] = 2^(m_k - M) are each computed once, spread over the
+// threads and kept in shared memory, so the per-dimension sums that follow
+// (sum_k wk[k] * o_k[d]) run over independent loads. Every thread returns M
+// and L = sum_k wk[k] * l_k. Ends with a barrier: red is free again, wk holds
+// the weights until the caller's next barrier.
+template <bool CACHED>
+__device__ __forceinline__ void merge_weights(const float* first, int n, size_t stride, float* wk, float* red,
+                                              float& M, float& L) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
+    auto ld = [](const float* x) { return CACHED ? __ldcg(x) : __ldg(x); };
+    float m = -INFINITY;
+    for (int k = t; k < n; k += blockDim.x) m = fmaxf(m, ld(first + k * stride));
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    M = red[0];
+    for (int w = 1; w < nw; ++w) M = fmaxf(M, red[w]);
+    float l = 0.f;
+    for (int k = t; k < n; k += blockDim.x) {
+        const float f = M == -INFINITY ? 0.f : exp2f(ld(first + k * stride) - M);
+        wk[k] = f;
+        l = fmaf(f, ld(first + k * stride + 1), l);
+    }
+    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+    __syncthreads();  // every thread has read the maxima in red
+    if (lane == 0) red[warp] = l;
+    __syncthreads();  // the sums are in red and the weights in wk
+    L = 0.f;
+    for (int w = 0; w < nw; ++w) L += red[w];
+    __syncthreads();  // red is reused by the next call
+}
+
+template <bool CACHED>
+__device__ __forceinline__ float merged_dim(const float* first, int n, size_t stride, const float* wk, int d) {
+    float acc = 0.f;
+#pragma unroll 4
+    for (int k = 0; k < n; ++k) acc = fmaf(wk[k], CACHED ? __ldcg(first + k * stride + 4 + d) : __ldg(first + k * stride + 4 + d), acc);
+    return acc;
+}
+
+// src: this rank's records, P consecutive records of D+4 floats per row (the
+// decode's split records; P == 1: one record per row).
+__global__ void __launch_bounds__(kP2PThreads) p2p_exchange_combine_kernel(
+    const float* __restrict__ src, int P, const P2PPeers peers, unsigned int* epochs, int nranks, int rank,
+    int rows, int D, int rows_per_b, void* out, int64_t o_sb, int64_t o_sh, uint32_t flags) {
     const int c = blockIdx.x, ctas = gridDim.x;
-    const int r0 = c * kP2PRows, r1 = min(rows, r0 + kP2PRows);
     const int rs = D + 4;
+    const int nblk = (rows + kP2PRows - 1) / kP2PRows;
     __shared__ unsigned int e_sh;
     __shared__ int ok_sh;
+    __shared__ float wk[kMaxMerge];
+    __shared__ float red[kP2PThreads / 32];
     if (threadIdx.x == 0) e_sh = ++epochs[c];
     __syncthreads();
     const unsigned int e = e_sh;
     const int par = static_cast<int>(e & 1u);
     const size_t slab = static_cast<size_t>(rows) * rs;  // one rank's records
-    // 1. push this CTA's rows of our records into every rank's buffer
-    const float4* src = reinterpret_cast<const float4*>(local + static_cast<size_t>(r0) * rs);
-    const int n4 = (r1 - r0) * rs / 4;
-    for (int p = 0; p < nranks; ++p) {
-        float4* dst = reinterpret_cast<float4*>(peers.gather[p] + (static_cast<size_t>(par) * nranks + rank) * slab +
-                                                static_cast<size_t>(r0) * rs);
-        for (int i = threadIdx.x; i < n4; i += blockDim.x) dst[i] = __ldg(src + i);
+    // 1. merge this rank's split records of every row of this CTA's blocks and
+    //    push the merged record into every rank's gather buffer
+    for (int blk = c; blk < nblk; blk += ctas) {
+        const int r1 = min(rows, (blk + 1) * kP2PRows);
+        for (int r = blk * kP2PRows; r < r1; ++r) {
+            const float* rec = src + static_cast<size_t>(r) * P * rs;
+            const size_t dst_off = (static_cast<size_t>(par) * nranks + rank) * slab + static_cast<size_t>(r) * rs;
+            if (P == 1) {
+                for (int i = threadIdx.x; i < rs / 4; i += blockDim.x) {
+                    const float4 v = __ldg(reinterpret_cast<const float4*>(rec) + i);
+                    for (int p = 0; p < nranks; ++p) reinterpret_cast<float4*>(peers.gather[p] + dst_off)[i] = v;
+                }
+                continue;
+            }
+            float M, L;
+            merge_weights<false>(rec, P, rs, wk, red, M, L);
+            for (int d = threadIdx.x; d < D; d += blockDim.x) {
+                const float O = merged_dim<false>(rec, P, rs, wk, d);
+                for (int p = 0; p < nranks; ++p) {
+                    float* dst = peers.gather[p] + dst_off;
+                    dst[4 + d] = O;
+                    if (d == 0) { dst[0] = M; dst[1] = L; }
+                }
+            }
+            __syncthreads();  // wk is rewritten by the next row
+        }
     }
     __syncthreads();
     // 2. publish: one release store per rank, ordered after every thread's stores
@@ -200,7 +275,7 @@ __global__ void __launch_bounds__(128) p2p_exchange_combine_kernel(
         __threadfence_system();
         st_release_sys(peers.flags[threadIdx.x] + static_cast<size_t>(rank) * ctas + c, e);
     }
-    // 3. wait for every rank's rows of this epoch (bounded)
+    // 3. wait for every rank's flag of this CTA and epoch (bounded)
     if (threadIdx.x == 0) ok_sh = 1;
     __syncthreads();
     if (threadIdx.x < nranks) {
@@ -218,25 +293,22 @@ __global__ void __launch_bounds__(128) p2p_exchange_combine_kernel(
         }
     }
     __syncthreads();
-    if (!ok_sh) return;
-    // 4. log-sum-exp merge of our rows (records read from L2: peers wrote them)
+    if (!ok_sh) return;  // a rank missed this call: these rows stay unwritten (the status says so)
+    // 4. log-sum-exp merge of this CTA's rows (records read from L2: peers wrote them)
     const float* mine = peers.gather[rank] + static_cast<size_t>(par) * nranks * slab;
-    for (int r = r0; r < r1; ++r) {
-        float M = -INFINITY;
-        for (int k = 0; k < nranks; ++k) M = fmaxf(M, __ldcg(mine + k * slab + static_cast<size_t>(r) * rs));
-        const int b = r / rows_per_b, h = r - b * rows_per_b;
-        const int64_t ro = b * o_sb + static_cast<int64_t>(h) * o_sh;
-        for (int d = threadIdx.x; d < D; d += blockDim.x) {
-            float O = 0.f, L = 0.f;
-            if (M != -INFINITY) {
-                for (int k = 0; k < nranks; ++k) {
-                    const float* rec = mine + k * slab + static_cast<size_t>(r) * rs;
-                    const float f = exp2f(__ldcg(rec) - M);
-                    O = fmaf(f, __ldcg(rec + 4 + d), O);
-                    L = fmaf(f, __ldcg(rec + 1), L);
-                }
+    for (int blk = c; blk < nblk; blk += ctas) {
+        const int r1 = min(rows, (blk + 1) * kP2PRows);
+        for (int r = blk * kP2PRows; r < r1; ++r) {
+            const float* first = mine + static_cast<size_t>(r) * rs;
+            float M, L;
+            merge_weights<true>(first, nranks, slab, wk, red, M, L);
+            const int b = r / rows_per_b, h = r - b * rows_per_b;
+            const int64_t ro = b * o_sb + static_cast<int64_t>(h) * o_sh;
+            for (int d = threadIdx.x; d < D; d += blockDim.x) {
+                const float O = merged_dim<true>(first, nranks, slab, wk, d);
+                store_out(out, ro + d, L > 0.f ? O / L : 0.f, flags);
             }
-            store_out(out, ro + d, L > 0.f ? O / L : 0.f, flags);
+            __syncthreads();  // wk is rewritten by the next row
         }
     }
 }
@@ -246,9 +318,11 @@ __global__ void __launch_bounds__(128) p2p_exchange_combine_kernel(
 
 struct kvd_mgpu_p2p {
     int nranks, rank, batch, heads, head_dim, rows, ctas;
-    size_t slab_floats;
+    size_t slab_floats, region_bytes;
+    void* comm;               // the communicator given at creation (reset barriers)
     void* region;             // this rank's gather buffer + flags (IPC-exported)
     unsigned int* epochs;     // local per-CTA epoch counters
+    int* barrier_buf;         // [nranks + 1] ints for the reset's NCCL barriers
     kvd::P2PPeers peers;
     void* opened[kvd::kMaxRanks];  // IPC mappings of the peers' regions
 };
@@ -261,16 +335,27 @@ extern "C" cudaError_t kvd_mgpu_p2p_create(kvd_mgpu_p2p** out, int batch, int nu
         return cudaErrorInvalidValue;
     const NcclApi& api = nccl();
     if (!api.ok) return cudaErrorSharedObjectInitFailed;
+    // Co-resident bound of the persistent exchange grid (every CTA must be able
+    // to run while the others wait).
+    int per_sm = 0;
+    cudaError_t e =
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, p2p_exchange_combine_kernel, kP2PThreads, 0);
+    if (e != cudaSuccess) return e;
+    const int64_t resident = static_cast<int64_t>(device_sm_count()) * (per_sm > 0 ? per_sm : 1);
     kvd_mgpu_p2p* c = new kvd_mgpu_p2p{};
     c->nranks = nranks; c->rank = rank; c->batch = batch; c->heads = num_q_heads; c->head_dim = head_dim;
+    c->comm = comm;
     c->rows = batch * num_q_heads;
-    c->ctas = (c->rows + kP2PRows - 1) / kP2PRows;
+    const int64_t nblk = (c->rows + kP2PRows - 1) / kP2PRows;
+    c->ctas = static_cast<int>(nblk < resident ? nblk : resident);
     c->slab_floats = static_cast<size_t>(c->rows) * (head_dim + 4);
     const size_t gather_bytes = align256(2 * static_cast<size_t>(nranks) * c->slab_floats * sizeof(float));
     const size_t flag_bytes = align256(static_cast<size_t>(nranks) * c->ctas * sizeof(unsigned int));
-    cudaError_t e = cudaMalloc(&c->region, gather_bytes + flag_bytes);
+    c->region_bytes = gather_bytes + flag_bytes;
+    e = cudaMalloc(&c->region, c->region_bytes);
     if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c->epochs), c->ctas * sizeof(unsigned int));
-    if (e == cudaSuccess) e = cudaMemset(c->region, 0, gather_bytes + flag_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c->barrier_buf), (nranks + 1) * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->region, 0, c->region_bytes);
     if (e == cudaSuccess) e = cudaMemset(c->epochs, 0, c->ctas * sizeof(unsigned int));
     cudaIpcMemHandle_t mine{};
     if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mine, c->region);
@@ -313,8 +398,37 @@ extern "C" cudaError_t kvd_mgpu_p2p_destroy(kvd_mgpu_p2p* c) {
         }
     if (c->region) cudaFree(c->region);
     if (c->epochs) cudaFree(c->epochs);
+    if (c->barrier_buf) cudaFree(c->barrier_buf);
     delete c;
     return first;
+}
+
+namespace {
+// Every rank of the context's communicator reaches this point before any
+// returns: an NCCL all-gather of one int, waited for on the host.
+cudaError_t p2p_barrier(kvd_mgpu_p2p* c, cudaStream_t stream) {
+    const kvd::NcclApi& api = kvd::nccl();
+    if (!api.ok) return cudaErrorSharedObjectInitFailed;
+    cudaError_t e = kvd::from_nccl(api.all_gather(c->barrier_buf + c->nranks, c->barrier_buf, 1, ncclInt32,
+                                                  static_cast<ncclComm_t>(c->comm), stream));
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    return e;
+}
+}  // namespace
+
+extern "C" cudaError_t kvd_mgpu_p2p_reset(kvd_mgpu_p2p* c, cudaStream_t stream) {
+    if (!c) return cudaErrorInvalidValue;
+    // 1. none of this rank's exchanges is still running
+    cudaError_t e = cudaDeviceSynchronize();
+    // 2. none of any rank's (every rank is past step 1)
+    if (e == cudaSuccess) e = p2p_barrier(c, stream);
+    // 3. epochs, flags and gather buffers back to their state at creation
+    if (e == cudaSuccess) e = cudaMemsetAsync(c->region, 0, c->region_bytes, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(c->epochs, 0, c->ctas * sizeof(unsigned int), stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    // 4. no rank pushes into a peer's buffers before that peer has cleared them
+    if (e == cudaSuccess) e = p2p_barrier(c, stream);
+    return e;
 }
 
 extern "C" size_t kvd_mgpu_p2p_workspace_size(const kvd_decode_desc* desc) {
@@ -328,7 +442,7 @@ extern "C" cudaError_t kvd_mgpu_p2p_seq_split_decode(kvd_mgpu_p2p* c, const kvd_
                                                      size_t workspace_bytes, cudaStream_t stream) {
     using namespace kvd;
     int* launches = launch_counter();
-    if (!c || !desc || !out || !workspace) return cudaErrorInvalidValue;
+    if (!c || !desc || !out || !workspace || !Q || !K || !V || !k_scale || !v_scale) return cudaErrorInvalidValue;
     if (desc->batch != c->batch || desc->num_q_heads != c->heads || desc->head_dim != c->head_dim ||
         (desc->flags & KVD_FLAG_PARTIAL_OUT))
         return cudaErrorInvalidValue;
@@ -339,12 +453,29 @@ extern "C" cudaError_t kvd_mgpu_p2p_seq_split_decode(kvd_mgpu_p2p* c, const kvd_
     char* ws = static_cast<char*>(workspace);
     float* local = reinterpret_cast<float*>(ws);
     char* dws = ws + 2 * rec;
-    cudaError_t e = kvd_decode_launch(&r, Q, K, V, k_scale, v_scale, local, dws, workspace_bytes - (dws - ws), stream);
-    if (e != cudaSuccess) return e;
-    int n = *launches;
-    p2p_exchange_combine_kernel<<<c->ctas, 128, 0, stream>>>(
-        local, c->peers, c->epochs, c->nranks, c->rank, c->rows, c->head_dim, c->heads, out, desc->o_stride_b,
-        desc->o_stride_h, desc->flags & (KVD_FLAG_OUT_BF16 | KVD_FLAG_OUT_F16));
+    const size_t dws_bytes = workspace_bytes - (dws - ws);
+    // 1. this rank's token range -> records. A dense tensor-core decode leaves
+    //    its split records in the workspace and the exchange kernel merges them,
+    //    so no separate combine launch runs.
+    SplitRecords splits{local, 1};
+    cudaError_t e;
+    int n = 0;
+    if (!r.seq_lens && fast_path_ok(r, Q, K, V) && gqa_path_ok(r)) {
+        e = launch_gqa_tc(r, Q, K, V, k_scale, v_scale, local, dws, dws_bytes, stream, &n, nullptr, nullptr,
+                          &splits);
+        if (splits.P == 1) splits.partials = local;
+    } else {
+        e = kvd_decode_launch(&r, Q, K, V, k_scale, v_scale, local, dws, dws_bytes, stream);
+        n = *launches;
+    }
+    if (e != cudaSuccess) {
+        *launches = n;
+        return e;
+    }
+    // 2. merge, push, wait, merge: one kernel
+    p2p_exchange_combine_kernel<<<c->ctas, kP2PThreads, 0, stream>>>(
+        splits.partials, splits.P, c->peers, c->epochs, c->nranks, c->rank, c->rows, c->head_dim, c->heads, out,
+        desc->o_stride_b, desc->o_stride_h, desc->flags & (KVD_FLAG_OUT_BF16 | KVD_FLAG_OUT_F16));
     e = cudaGetLastError();
     if (e == cudaSuccess) ++n;
     *launches = n;

@@ -163,6 +163,7 @@ _SIGNATURES = {
                                   + [c_void_p, c_size_t, c_void_p, c_int, c_void_p]),
     "kvd_mgpu_p2p_create": (c_int, [ctypes.POINTER(c_void_p), c_int, c_int, c_int, c_void_p, c_int, c_int]),
     "kvd_mgpu_p2p_destroy": (c_int, [c_void_p]),
+    "kvd_mgpu_p2p_reset": (c_int, [c_void_p, c_void_p]),
     "kvd_mgpu_p2p_workspace_size": (c_size_t, [ctypes.POINTER(DecodeDesc)]),
     "kvd_mgpu_p2p_seq_split_decode": (c_int, [c_void_p, ctypes.POINTER(DecodeDesc)] + [c_void_p] * 6
                                       + [c_void_p, c_size_t, c_void_p]),
@@ -599,6 +600,11 @@ class P2PExchange:
                                                  _stream(stream))
         _check(rc, "kvd_mgpu_p2p_seq_split_decode")
         return out
+
+    def reset(self, stream=None) -> None:
+        """Collective: clears the exchange state on every rank after a call timed
+        out (KVD_STATUS_WAIT_TIMEOUT), so the ranks' calls pair up again."""
+        _check(lib().kvd_mgpu_p2p_reset(self.handle, _stream(stream)), "kvd_mgpu_p2p_reset")
 
     def close(self) -> None:
         if self.handle:

@@ -318,18 +318,28 @@ cudaError_t kvd_mgpu_seq_split_decode(const kvd_decode_desc* desc,
 
 /* The same sequence split with the record exchange done by the library's own
  * kernel over NVLink instead of NCCL: after the local decode, one kernel
- * stores this rank's records straight into every rank's gather buffer (CUDA
- * IPC mappings of peer memory), raises a flag per (rank, row block) in each
- * peer's memory, waits for all ranks' flags of its rows (bounded: a rank that
- * never arrives turns into KVD_STATUS_WAIT_TIMEOUT after 2 s) and merges them.
+ * merges this rank's split records of each row, stores the merged record
+ * straight into every rank's gather buffer (CUDA IPC mappings of peer memory),
+ * raises a flag per (rank, CTA) in each peer's memory, waits for all ranks'
+ * flags (bounded: a rank that never arrives turns into KVD_STATUS_WAIT_TIMEOUT
+ * after 2 s) and merges the gathered records. The exchange kernel never runs
+ * more CTAs than fit on the GPU at once, so any batch size completes.
  * kvd_mgpu_p2p_create is collective (every rank calls it with the same sizes):
  * it allocates the exchange buffers (cudaMalloc) and swaps IPC handles once
- * over `comm`. Up to 8 ranks, head_dim a multiple of 4. Every rank must make
- * the same sequence of decode calls. */
+ * over `comm`, which must outlive the context. Up to 8 ranks, head_dim a
+ * multiple of 4. Every rank must make the same sequence of decode calls.
+ *
+ * After a call that recorded KVD_STATUS_WAIT_TIMEOUT (a rank missed a call or
+ * stalled), the rows of the timed-out CTAs are not written and the ranks' call
+ * counts no longer agree: every later call would pair records of different
+ * steps. Call kvd_mgpu_p2p_reset on every rank (collective over `comm`; it
+ * synchronises the device, clears the exchange state between two barriers)
+ * before the next decode, or destroy and recreate the context. */
 typedef struct kvd_mgpu_p2p kvd_mgpu_p2p;
 cudaError_t kvd_mgpu_p2p_create(kvd_mgpu_p2p** ctx, int batch, int num_q_heads, int head_dim,
                                 void* comm, int nranks, int rank);
 cudaError_t kvd_mgpu_p2p_destroy(kvd_mgpu_p2p* ctx);
+cudaError_t kvd_mgpu_p2p_reset(kvd_mgpu_p2p* ctx, cudaStream_t stream);
 size_t kvd_mgpu_p2p_workspace_size(const kvd_decode_desc* desc);
 cudaError_t kvd_mgpu_p2p_seq_split_decode(kvd_mgpu_p2p* ctx, const kvd_decode_desc* desc,
                                           const void* Q, const int8_t* K, const int8_t* V,

@@ -7,6 +7,7 @@ Exits 0 only if every rank's results are within the decode tolerance."""
 import datetime
 import os
 import sys
+import time
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path[:0] = [os.path.join(ROOT, "cuda-operators_b200"), os.path.join(ROOT, "oracle")]
@@ -18,6 +19,44 @@ import torch.distributed as dist  # noqa: E402
 import kvd_mgpu as mg  # noqa: E402
 import kvdecode as kvd  # noqa: E402
 import pyoracle as po  # noqa: E402
+
+
+def missed_call_then_reset(comm, rank: int, world: int, dev) -> int:
+    """A rank that misses one exchange call (a dropped step, injected on the
+    host): rank 0's call must end with KVD_STATUS_WAIT_TIMEOUT within a few
+    seconds instead of hanging, and after the collective reset every rank's next
+    calls must match the oracle again."""
+    bad = 0
+    B, Hq, S = 2, 8, 4096
+    q, K, V, ks, vs = po.random_cache(37, B, Hq, Hq, S, 128)
+    ref = po.decode_f64(q, K, V, ks, vs)
+    lo, hi = mg.seq_shard(S, world, rank, align=128)
+    shard = [torch.from_numpy(np.ascontiguousarray(a[:, :, lo:hi])).to(dev) for a in (K, V, ks, vs)]
+    tq = torch.from_numpy(q).to(dev)
+    ex = kvd.P2PExchange(comm, B, Hq, 128)
+    try:
+        out = ex.decode(tq, *shard)  # every rank: epoch 1
+        torch.cuda.synchronize()
+        bad += po.check(out.cpu().numpy(), ref)[0]
+        if rank == 0:  # the other ranks skip this call
+            t0 = time.time()
+            ex.decode(tq, *shard)
+            st = kvd.device_status()
+            dt = time.time() - t0
+            print(f"[rank 0] call missed by the peers: status={st} after {dt:.2f} s", flush=True)
+            bad += int(not (st & kvd.KVD_STATUS_WAIT_TIMEOUT)) + int(dt > 10.0)
+        ex.reset()  # collective: the ranks meet here, then clear their exchange state
+        for step in range(3):
+            out = ex.decode(tq, *shard)
+            torch.cuda.synchronize()
+            b, err, _ = po.check(out.cpu().numpy(), ref)
+            bad += b
+            print(f"[rank {rank}] after reset, step {step}: max_abs={err:.3g} bad={b}", flush=True)
+        bad += int(kvd.device_status() != kvd.KVD_STATUS_OK)
+    finally:
+        dist.barrier()
+        ex.close()
+    return bad
 
 
 def main() -> int:
@@ -97,6 +136,7 @@ def main() -> int:
                 finally:
                     dist.barrier()  # no rank unmaps its buffers while a peer could still write them
                     ex.close()
+            bad += missed_call_then_reset(comm, rank, world, dev)
         finally:
             comm.close()
         flag = torch.tensor([bad], device=dev)
