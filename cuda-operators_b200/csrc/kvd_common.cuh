@@ -165,6 +165,14 @@ __device__ __forceinline__ void dequant4(uint32_t w, float2& lo, float2& hi) {
     hi = __fadd2_rn(make_float2(f2, f3), m);
 }
 
+// Programmatic dependent launch. A kernel launched with the programmatic
+// stream-serialization attribute may start while the kernel before it in the
+// stream is still running; grid_dependency_wait() blocks until that kernel has
+// completed and its memory writes are visible (a no-op without the attribute).
+// allow_dependents() lets such a dependent kernel begin launching early.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float fast_exp2(float x) {
     return exp2f(x);
 }

@@ -165,6 +165,7 @@ __global__ void __launch_bounds__(kGenThreads) generic_decode_kernel(const GenPa
 __global__ void __launch_bounds__(128) combine_records_kernel(
     const float* base, int nparts, int64_t part_stride, int64_t rec_stride, int rows_per_b, int D,
     void* out, int64_t o_sb, int64_t o_sh, uint32_t flags) {
+    grid_dependency_wait();  // when launched as a programmatic dependent of the decode that wrote the records
     const int64_t r = blockIdx.x;
     const float* first = base + r * rec_stride;
     float M = -INFINITY;
@@ -286,9 +287,19 @@ cudaError_t launch_generic_prefill(const kvd_prefill_desc& d, const void* Q, con
 cudaError_t launch_combine_records(const float* base, int nparts, int64_t part_stride, int64_t rec_stride,
                                    int64_t rows, int rows_per_b, int D, void* out, int64_t o_sb, int64_t o_sh,
                                    uint32_t flags, cudaStream_t st, int* launches) {
-    combine_records_kernel<<<static_cast<unsigned>(rows), 128, 0, st>>>(base, nparts, part_stride, rec_stride,
-                                                                         rows_per_b, D, out, o_sb, o_sh, flags);
-    const cudaError_t e = cudaGetLastError();
+    // Programmatic dependent of the decode that wrote the records: its CTAs may be
+    // scheduled as the decode's retire; each waits for the decode's completion first.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(rows), 1, 1);
+    cfg.blockDim = dim3(128, 1, 1);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, combine_records_kernel, base, nparts, part_stride, rec_stride,
+                                             rows_per_b, D, out, o_sb, o_sh, flags);
     if (e == cudaSuccess) ++*launches;
     return e;
 }

@@ -949,6 +949,10 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV, QM>::THREADS, MINB) gqa_tc_k
     constexpr int EW = 4 * C::NWG;  // epilogue warps; then the producer warp, then the MMA warp
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    // A follow-up kernel launched as a programmatic dependent (the split combine,
+    // the multi-GPU record exchange) may be scheduled onto SMs as this grid's
+    // CTAs retire; it waits for this grid's completion before reading its output.
+    allow_dependents();
     if (next_item(p, blockIdx.x) >= p.n_items) {  // no (non-empty) item for this CTA
         if (p.k_new) fused_append_finish(p);
         return;

@@ -237,6 +237,7 @@ __global__ void __launch_bounds__(kP2PThreads) p2p_exchange_combine_kernel(
     __shared__ int ok_sh;
     __shared__ float wk[kMaxMerge];
     __shared__ float red[kP2PThreads / 32];
+    grid_dependency_wait();  // launched as a programmatic dependent of the local decode: its records are complete
     if (threadIdx.x == 0) e_sh = ++epochs[c];
     __syncthreads();
     const unsigned int e = e_sh;
@@ -473,10 +474,21 @@ extern "C" cudaError_t kvd_mgpu_p2p_seq_split_decode(kvd_mgpu_p2p* c, const kvd_
         return e;
     }
     // 2. merge, push, wait, merge: one kernel
-    p2p_exchange_combine_kernel<<<c->ctas, kP2PThreads, 0, stream>>>(
-        splits.partials, splits.P, c->peers, c->epochs, c->nranks, c->rank, c->rows, c->head_dim, c->heads, out,
-        desc->o_stride_b, desc->o_stride_h, desc->flags & (KVD_FLAG_OUT_BF16 | KVD_FLAG_OUT_F16));
-    e = cudaGetLastError();
+    // Programmatic dependent launch: the exchange's CTAs may be scheduled while the
+    // decode's last CTAs run and wait (griddepcontrol.wait) for its completion.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(c->ctas), 1, 1);
+    cfg.blockDim = dim3(kP2PThreads, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, p2p_exchange_combine_kernel, static_cast<const float*>(splits.partials), splits.P,
+                           c->peers, c->epochs, c->nranks, c->rank, c->rows, c->head_dim, c->heads, out,
+                           static_cast<int64_t>(desc->o_stride_b), static_cast<int64_t>(desc->o_stride_h),
+                           static_cast<uint32_t>(desc->flags & (KVD_FLAG_OUT_BF16 | KVD_FLAG_OUT_F16)));
     if (e == cudaSuccess) ++n;
     *launches = n;
     return e;
