@@ -1,8 +1,11 @@
 // kvd_abi.cu -- the extern "C" boundary of libkvdecode_b200.so: argument
 // checks, path selection, workspace planning and the reference-compatible
 // entry points (see include/kvdecode.h for the contract of each symbol).
+#include <cuda.h>
+
 #include <cstdio>
 #include <cstdint>
+#include <mutex>
 
 #include "kvd_common.cuh"
 #include "kvd_decode.cuh"
@@ -16,6 +19,22 @@ cudaError_t launch_append(const kvd_append_desc& d, const float* k_new, const fl
                           int8_t* V, float* ks, float* vs, int32_t* seq_lens, cudaStream_t st);
 cudaError_t launch_quantize_rows(const float* x, int64_t rows, int dim, int64_t x_stride, int8_t* codes,
                                  int64_t code_stride, float* scales, int sms, cudaStream_t st);
+
+unsigned long long current_context_id() {
+    using Fn = CUresult (*)(CUcontext, unsigned long long*);
+    static Fn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {  // through the runtime, so the library does not link the driver library
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<Fn>(ptr);
+    });
+    unsigned long long id = 0;
+    if (!fn || fn(nullptr, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
 
 int device_sm_count() {
     static std::atomic<int> cache[kMaxDevices] = {};

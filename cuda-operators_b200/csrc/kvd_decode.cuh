@@ -16,9 +16,14 @@ namespace kvd {
 // cached SM counts); calls on higher ordinals return cudaErrorInvalidDevice.
 constexpr int kMaxDevices = 64;
 
-// Runs a set-up step (a kernel attribute) once per device, for the device
-// current on the calling thread. Thread-safe: concurrent first calls wait for
-// one another; a failed step is retried by the next call.
+// Unique id of the calling thread's current CUDA context (ids are never reused
+// within a process), or 0 when none is current yet.
+unsigned long long current_context_id();
+
+// Runs a set-up step (a kernel attribute) once per device and CUDA context,
+// for the device current on the calling thread: a new context of the device
+// (after cudaDeviceReset) runs it again. Thread-safe: concurrent first calls
+// wait for one another; a failed step is retried by the next call.
 class PerDeviceOnce {
 public:
     template <class F>
@@ -27,17 +32,18 @@ public:
         cudaError_t e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return e;
         if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-        if (done_[dev].load(std::memory_order_acquire)) return cudaSuccess;
+        const unsigned long long ctx = current_context_id();
+        if (ctx != 0 && done_[dev].load(std::memory_order_acquire) == ctx) return cudaSuccess;
         std::lock_guard<std::mutex> lock(mu_);
-        if (done_[dev].load(std::memory_order_relaxed)) return cudaSuccess;
-        e = fn();
-        if (e == cudaSuccess) done_[dev].store(true, std::memory_order_release);
+        if (ctx != 0 && done_[dev].load(std::memory_order_relaxed) == ctx) return cudaSuccess;
+        e = fn();  // binds the device's primary context if none was current
+        if (e == cudaSuccess) done_[dev].store(current_context_id(), std::memory_order_release);
         return e;
     }
 
 private:
     std::mutex mu_;
-    std::atomic<bool> done_[kMaxDevices] = {};
+    std::atomic<unsigned long long> done_[kMaxDevices] = {};  // context id the step last ran in
 };
 
 // One-launch small-problem decode (kvd_small.cu): at most kSmallMaxCluster

@@ -54,26 +54,6 @@ struct NoallocSlot {
 std::mutex g_noalloc_mutex;
 NoallocSlot g_noalloc_slots[kMaxDevices] = {};
 
-// Unique id of the calling thread's current CUDA context (cuCtxGetId: ids are
-// never reused within a process), or 0 when none is current yet or the driver
-// lacks the call. Resolved through the runtime, so the library does not link
-// the driver library.
-unsigned long long current_context_id() {
-    using Fn = CUresult (*)(CUcontext, unsigned long long*);
-    static Fn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* ptr = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuCtxGetId", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<Fn>(ptr);
-    });
-    unsigned long long id = 0;
-    if (!fn || fn(nullptr, &id) != CUDA_SUCCESS) return 0;
-    return id;
-}
-
 // Device address of g_noalloc_scratch in the current context (host code sees
 // only a host-side stand-in for the symbol; it must never be passed to a kernel).
 cudaError_t noalloc_scratch_address(void** out) {

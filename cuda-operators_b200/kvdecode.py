@@ -455,7 +455,7 @@ def quantize_rows(x, codes=None, scales=None, stream=None):
 
 # ------------------------------------------------------------------ paged cache
 def make_paged_desc(q, k_pool, ks_pool, out, block_table, seq_lens, layout: str = "bhtd",
-                    softmax_scale: float = 0.0, partial: bool = False) -> PagedDesc:
+                    softmax_scale: float = 0.0, partial: bool = False, qk_int8: bool = False) -> PagedDesc:
     """Descriptor for a paged cache. ``k_pool`` is [blocks, Hkv, block_size, D]
     (layout "bhtd") or [blocks, block_size, Hkv, D] (layout "bthd"); scale pools
     are [blocks, Hkv, block_size]; ``block_table`` is int32 [B, max_blocks]."""
@@ -477,7 +477,7 @@ def make_paged_desc(q, k_pool, ks_pool, out, block_table, seq_lens, layout: str 
     d = PagedDesc()
     d.batch, d.num_q_heads, d.num_kv_heads, d.head_dim = B, Hq, Hkv, D
     d.block_size, d.num_blocks, d.max_blocks_per_seq = bs, NB, block_table.shape[1]
-    d.flags = dtype_flags(q if q.device.type != "meta" else None, out, partial)
+    d.flags = dtype_flags(q if q.device.type != "meta" else None, out, partial) | (KVD_FLAG_QK_INT8 if qk_int8 else 0)
     d.seq_lens, d.block_table = _ptr(seq_lens), _ptr(block_table)
     d.block_table_stride = block_table.stride(0)
     d.kv_stride_block, d.kv_stride_h, d.kv_stride_t = s_blk, s_h, s_t
@@ -493,7 +493,8 @@ def paged_workspace_size(desc: PagedDesc) -> int:
 
 
 def paged_decode(q, k_pool, v_pool, ks_pool, vs_pool, block_table, seq_lens, out=None, layout: str = "bhtd",
-                 softmax_scale: float = 0.0, partial: bool = False, workspace=None, stream=None, out_dtype=None):
+                 softmax_scale: float = 0.0, partial: bool = False, workspace=None, stream=None, out_dtype=None,
+                 qk_int8: bool = False):
     """INT8 decode attention over a paged cache; returns ``out`` [B,Hq,D] (or records)."""
     import torch
 
@@ -502,7 +503,7 @@ def paged_decode(q, k_pool, v_pool, ks_pool, vs_pool, block_table, seq_lens, out
         out = torch.empty((B, Hq, D + 4 if partial else D), dtype=out_dtype or torch.float32, device=q.device)
     if v_pool.stride() != k_pool.stride() or vs_pool.stride() != ks_pool.stride():
         raise ValueError("K/V pools and their scale pools must share strides")
-    desc = make_paged_desc(q, k_pool, ks_pool, out, block_table, seq_lens, layout, softmax_scale, partial)
+    desc = make_paged_desc(q, k_pool, ks_pool, out, block_table, seq_lens, layout, softmax_scale, partial, qk_int8)
     if workspace is None:
         workspace = torch.empty(max(paged_workspace_size(desc), 1), dtype=torch.uint8, device=q.device)
     rc = lib().kvd_paged_decode_launch(ctypes.byref(desc), _ptr(q), _ptr(k_pool), _ptr(v_pool), _ptr(ks_pool),

@@ -117,3 +117,27 @@ def test_qk_int8_outside_the_tensor_core_kernel_is_not_supported():
     with pytest.raises(kvd.KvdError) as ei:
         kvd.decode(q, K, V, ks, vs, qk_int8=True)
     assert ei.value.code == 801  # cudaErrorNotSupported
+
+
+@pytest.mark.parametrize("bs,layout", [(16, "bhtd"), (64, "bthd")])
+def test_qk_int8_paged_cache(bs, layout):
+    """The INT8 Q.K mode through the paged entry point: the same bits as the
+    dense ragged decode of the cache the pools were scattered from, and exact
+    attention of the rounded query."""
+    from test_paged import scatter_to_pool
+
+    B, Hq, Hkv, D = 3, 32, 4, 128
+    lens = np.array([1100, 0, 517], np.int32)
+    nb = -(-1100 // bs)
+    q, K, V, ks, vs = po.random_cache(97 + bs, B, Hq, Hkv, nb * bs, D)
+    Kp, Vp, ksp, vsp, table = scatter_to_pool(K, V, ks, vs, bs, layout, seed=5)
+    tq, tK, tV, tks, tvs, tl = (torch.from_numpy(np.ascontiguousarray(a)).to(DEV) for a in (q, K, V, ks, vs, lens))
+    pK, pV, pks, pvs, tt = (torch.from_numpy(np.ascontiguousarray(a)).to(DEV) for a in (Kp, Vp, ksp, vsp, table))
+    paged = kvd.paged_decode(tq, pK, pV, pks, pvs, tt, tl, layout=layout, qk_int8=True)
+    dense = kvd.decode(tq, tK, tV, tks, tvs, seq_lens=tl, qk_int8=True)
+    torch.cuda.synchronize()
+    assert np.array_equal(paged.cpu().numpy(), dense.cpu().numpy())
+    ref_hat = po.decode_f64(_rounded_query(q), K, V, ks, vs, seq_lens=lens)
+    bad, max_abs, _ = po.check(paged.cpu().numpy(), ref_hat, ATOL, RTOL)
+    assert bad == 0, f"{bad} bad, max abs {max_abs:.3g}"
+    assert kvd.device_status() == kvd.KVD_STATUS_OK

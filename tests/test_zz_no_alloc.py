@@ -8,6 +8,8 @@ oracle) within the decode tolerance, on two calls in a row, so stale contents
 left in the shared array by one call cannot change the next one's result.
 This file is collected last on purpose; it passes alone and after the rest."""
 import ctypes
+import subprocess
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -96,3 +98,25 @@ def test_noalloc_rejects_scratch_beyond_its_fixed_size():
     assert rc == kvd.CUDA_ERROR_INVALID_VALUE
     torch.cuda.synchronize()
     assert torch.all(out == 7.0)  # nothing was launched
+
+
+def test_noalloc_after_device_reset_in_a_process_of_its_own():
+    """A caller that resets its device (cudaDeviceReset) gets a new CUDA context;
+    the library must look the fixed array's address up again rather than use
+    the stale one. Runs as its own program, because a reset destroys every
+    allocation of the process: two rounds of (allocate, decode through the
+    workspace entry, decode twice through the no-alloc entry, compare, reset)."""
+    native = Path(__file__).resolve().parent / "native"
+    root = native.parents[1]
+    pkg = root / "cuda-operators_b200"
+    kvd.lib()
+    exe = native / "_build" / "noalloc_reset"
+    src = native / "noalloc_reset.cu"
+    if not exe.exists() or exe.stat().st_mtime < max(src.stat().st_mtime, kvd.LIB_PATH.stat().st_mtime):
+        exe.parent.mkdir(exist_ok=True)
+        subprocess.run(["nvcc", "-O2", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
+                        f"-I{root / 'include'}", str(src), f"-L{pkg}", "-lkvdecode_b200",
+                        f"-Xlinker=-rpath,{pkg}", "-o", str(exe)], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert r.stdout.count("max |noalloc - workspace entry|") == 4 and r.stdout.strip().endswith("ok"), r.stdout
