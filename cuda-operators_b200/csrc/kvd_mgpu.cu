@@ -319,8 +319,9 @@ __global__ void __launch_bounds__(kP2PThreads) p2p_exchange_combine_kernel(
 
 struct kvd_mgpu_p2p {
     int nranks, rank, batch, heads, head_dim, rows, ctas;
+    int device;               // the rank's device
     size_t slab_floats, region_bytes;
-    void* comm;               // the communicator given at creation (reset barriers)
+    void* comm;               // the communicator given at creation (reset barriers); nullptr in a group
     void* region;             // this rank's gather buffer + flags (IPC-exported)
     unsigned int* epochs;     // local per-CTA epoch counters
     int* barrier_buf;         // [nranks + 1] ints for the reset's NCCL barriers
@@ -346,6 +347,7 @@ extern "C" cudaError_t kvd_mgpu_p2p_create(kvd_mgpu_p2p** out, int batch, int nu
     kvd_mgpu_p2p* c = new kvd_mgpu_p2p{};
     c->nranks = nranks; c->rank = rank; c->batch = batch; c->heads = num_q_heads; c->head_dim = head_dim;
     c->comm = comm;
+    cudaGetDevice(&c->device);
     c->rows = batch * num_q_heads;
     const int64_t nblk = (c->rows + kP2PRows - 1) / kP2PRows;
     c->ctas = static_cast<int>(nblk < resident ? nblk : resident);
@@ -391,6 +393,9 @@ extern "C" cudaError_t kvd_mgpu_p2p_create(kvd_mgpu_p2p** out, int batch, int nu
 
 extern "C" cudaError_t kvd_mgpu_p2p_destroy(kvd_mgpu_p2p* c) {
     if (!c) return cudaErrorInvalidValue;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(c->device);
     cudaError_t first = cudaDeviceSynchronize();
     for (int p = 0; p < c->nranks; ++p)
         if (c->opened[p]) {
@@ -401,7 +406,82 @@ extern "C" cudaError_t kvd_mgpu_p2p_destroy(kvd_mgpu_p2p* c) {
     if (c->epochs) cudaFree(c->epochs);
     if (c->barrier_buf) cudaFree(c->barrier_buf);
     delete c;
+    cudaSetDevice(prev);
     return first;
+}
+
+extern "C" cudaError_t kvd_mgpu_p2p_create_group(kvd_mgpu_p2p** ctxs, int nranks, const int* devices, int batch,
+                                                 int num_q_heads, int head_dim) {
+    using namespace kvd;
+    if (!ctxs || !devices || batch < 1 || num_q_heads < 1 || head_dim < 1 || (head_dim & 3) != 0 || nranks < 1 ||
+        nranks > kMaxRanks)
+        return cudaErrorInvalidValue;
+    for (int r = 0; r < nranks; ++r) ctxs[r] = nullptr;
+    int prev = 0;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return e;
+    const int rows = batch * num_q_heads;
+    int64_t ctas = (rows + kP2PRows - 1) / kP2PRows;
+    // every rank runs the same grid: the co-resident bound of the smallest device
+    for (int r = 0; r < nranks && e == cudaSuccess; ++r) {
+        e = cudaSetDevice(devices[r]);
+        int per_sm = 0;
+        if (e == cudaSuccess)
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, p2p_exchange_combine_kernel, kP2PThreads, 0);
+        const int64_t resident = static_cast<int64_t>(device_sm_count()) * (per_sm > 0 ? per_sm : 1);
+        if (resident < ctas) ctas = resident;
+    }
+    // direct peer access between the distinct devices of the group
+    for (int r = 0; r < nranks && e == cudaSuccess; ++r)
+        for (int q = 0; q < nranks && e == cudaSuccess; ++q) {
+            if (devices[q] == devices[r]) continue;
+            int can = 0;
+            e = cudaDeviceCanAccessPeer(&can, devices[r], devices[q]);
+            if (e == cudaSuccess && !can) e = cudaErrorPeerAccessUnsupported;
+            if (e == cudaSuccess) e = cudaSetDevice(devices[r]);
+            if (e == cudaSuccess) {
+                e = cudaDeviceEnablePeerAccess(devices[q], 0);
+                if (e == cudaErrorPeerAccessAlreadyEnabled) {
+                    cudaGetLastError();  // already enabled (by the caller or an earlier group): fine
+                    e = cudaSuccess;
+                }
+            }
+        }
+    const size_t slab = static_cast<size_t>(rows) * (head_dim + 4);
+    const size_t gather_bytes = align256(2 * static_cast<size_t>(nranks) * slab * sizeof(float));
+    const size_t flag_bytes = align256(static_cast<size_t>(nranks) * ctas * sizeof(unsigned int));
+    for (int r = 0; r < nranks && e == cudaSuccess; ++r) {
+        e = cudaSetDevice(devices[r]);
+        if (e != cudaSuccess) break;
+        kvd_mgpu_p2p* c = new kvd_mgpu_p2p{};
+        ctxs[r] = c;
+        c->nranks = nranks; c->rank = r; c->batch = batch; c->heads = num_q_heads; c->head_dim = head_dim;
+        c->device = devices[r];
+        c->comm = nullptr;
+        c->rows = rows;
+        c->ctas = static_cast<int>(ctas);
+        c->slab_floats = slab;
+        c->region_bytes = gather_bytes + flag_bytes;
+        e = cudaMalloc(&c->region, c->region_bytes);
+        if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c->epochs), c->ctas * sizeof(unsigned int));
+        if (e == cudaSuccess) e = cudaMemset(c->region, 0, c->region_bytes);
+        if (e == cudaSuccess) e = cudaMemset(c->epochs, 0, c->ctas * sizeof(unsigned int));
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    }
+    for (int r = 0; r < nranks && e == cudaSuccess; ++r)
+        for (int q = 0; q < nranks; ++q) {
+            ctxs[r]->peers.gather[q] = static_cast<float*>(ctxs[q]->region);
+            ctxs[r]->peers.flags[q] = reinterpret_cast<unsigned int*>(static_cast<char*>(ctxs[q]->region) + gather_bytes);
+        }
+    if (e != cudaSuccess) {
+        for (int r = 0; r < nranks; ++r)
+            if (ctxs[r]) {
+                kvd_mgpu_p2p_destroy(ctxs[r]);
+                ctxs[r] = nullptr;
+            }
+    }
+    cudaSetDevice(prev);
+    return e;
 }
 
 namespace {
@@ -419,6 +499,17 @@ cudaError_t p2p_barrier(kvd_mgpu_p2p* c, cudaStream_t stream) {
 
 extern "C" cudaError_t kvd_mgpu_p2p_reset(kvd_mgpu_p2p* c, cudaStream_t stream) {
     if (!c) return cudaErrorInvalidValue;
+    if (!c->comm) {  // a single-process group: the caller resets every rank with no decode in flight
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaError_t e = cudaSetDevice(c->device);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e == cudaSuccess) e = cudaMemset(c->region, 0, c->region_bytes);
+        if (e == cudaSuccess) e = cudaMemset(c->epochs, 0, c->ctas * sizeof(unsigned int));
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        cudaSetDevice(prev);
+        return e;
+    }
     // 1. none of this rank's exchanges is still running
     cudaError_t e = cudaDeviceSynchronize();
     // 2. none of any rank's (every rank is past step 1)

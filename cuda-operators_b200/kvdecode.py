@@ -164,6 +164,7 @@ _SIGNATURES = {
     "kvd_mgpu_p2p_create": (c_int, [ctypes.POINTER(c_void_p), c_int, c_int, c_int, c_void_p, c_int, c_int]),
     "kvd_mgpu_p2p_destroy": (c_int, [c_void_p]),
     "kvd_mgpu_p2p_reset": (c_int, [c_void_p, c_void_p]),
+    "kvd_mgpu_p2p_create_group": (c_int, [ctypes.POINTER(c_void_p), c_int, ctypes.POINTER(c_int), c_int, c_int, c_int]),
     "kvd_mgpu_p2p_workspace_size": (c_size_t, [ctypes.POINTER(DecodeDesc)]),
     "kvd_mgpu_p2p_seq_split_decode": (c_int, [c_void_p, ctypes.POINTER(DecodeDesc)] + [c_void_p] * 6
                                       + [c_void_p, c_size_t, c_void_p]),
@@ -611,6 +612,50 @@ class P2PExchange:
         if self.handle:
             lib().kvd_mgpu_p2p_destroy(self.handle)
             self.handle = None
+
+
+class P2PGroup:
+    """Single-process sequence split (kvd_mgpu_p2p_create_group): one context per
+    rank, rank r on device devices[r], linked by direct peer pointers."""
+
+    def __init__(self, devices, batch: int, num_q_heads: int, head_dim: int):
+        n = len(devices)
+        hs = (c_void_p * n)()
+        devs = (c_int * n)(*devices)
+        _check(lib().kvd_mgpu_p2p_create_group(hs, n, devs, batch, num_q_heads, head_dim),
+               "kvd_mgpu_p2p_create_group")
+        self.handles = [hs[r] for r in range(n)]
+        self.devices = list(devices)
+        self._ws = {}
+
+    def decode(self, rank: int, q, k, v, ks, vs, out=None, seq_lens=None, stream=None, out_dtype=None):
+        """Launches rank `rank`'s step on its device (tensors on that device); returns without waiting."""
+        import torch
+
+        with torch.cuda.device(self.devices[rank]):
+            B, Hq, D = q.shape
+            if out is None:
+                out = torch.empty((B, Hq, D), dtype=out_dtype or torch.float32, device=q.device)
+            desc = make_desc(q, k, ks, out, seq_lens)
+            n = int(lib().kvd_mgpu_p2p_workspace_size(ctypes.byref(desc)))
+            ws = self._ws.get(rank)
+            if ws is None or ws.numel() < n:
+                ws = self._ws[rank] = torch.empty(max(n, 1), dtype=torch.uint8, device=q.device)
+            rc = lib().kvd_mgpu_p2p_seq_split_decode(self.handles[rank], ctypes.byref(desc), _ptr(q), _ptr(k),
+                                                     _ptr(v), _ptr(ks), _ptr(vs), _ptr(out), _ptr(ws), ws.numel(),
+                                                     _stream(stream))
+        _check(rc, "kvd_mgpu_p2p_seq_split_decode")
+        return out
+
+    def reset(self) -> None:
+        for h in self.handles:
+            _check(lib().kvd_mgpu_p2p_reset(h, None), "kvd_mgpu_p2p_reset")
+
+    def close(self) -> None:
+        for h in self.handles:
+            if h:
+                lib().kvd_mgpu_p2p_destroy(h)
+        self.handles = []
 
 
 def device_status() -> int:

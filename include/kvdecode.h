@@ -340,6 +340,18 @@ cudaError_t kvd_mgpu_p2p_create(kvd_mgpu_p2p** ctx, int batch, int num_q_heads, 
                                 void* comm, int nranks, int rank);
 cudaError_t kvd_mgpu_p2p_destroy(kvd_mgpu_p2p* ctx);
 cudaError_t kvd_mgpu_p2p_reset(kvd_mgpu_p2p* ctx, cudaStream_t stream);
+
+/* The same exchange for ONE process (or host thread) driving several GPUs: the
+ * contexts of all `nranks` ranks are made at once, rank r's on device
+ * devices[r], and linked by direct peer pointers (peer access is enabled
+ * between distinct devices; no IPC, no NCCL). ctxs[r] is used with
+ * kvd_mgpu_p2p_seq_split_decode while devices[r] is the current device; the
+ * ranks' calls must run concurrently (e.g. one stream per GPU, launched from
+ * one thread), since each waits for the others' records (bounded, as above).
+ * kvd_mgpu_p2p_reset on a group context needs no communicator: the caller
+ * resets every rank's context with no decode in flight. Destroy each context. */
+cudaError_t kvd_mgpu_p2p_create_group(kvd_mgpu_p2p** ctxs, int nranks, const int* devices, int batch,
+                                      int num_q_heads, int head_dim);
 size_t kvd_mgpu_p2p_workspace_size(const kvd_decode_desc* desc);
 cudaError_t kvd_mgpu_p2p_seq_split_decode(kvd_mgpu_p2p* ctx, const kvd_decode_desc* desc,
                                           const void* Q, const int8_t* K, const int8_t* V,
