@@ -540,6 +540,8 @@ extern "C" cudaError_t kvd_mgpu_p2p_seq_split_decode(kvd_mgpu_p2p* c, const kvd_
         return cudaErrorInvalidValue;
     const size_t need = kvd_mgpu_p2p_workspace_size(desc);
     if (need == 0 || workspace_bytes < need) return cudaErrorInvalidValue;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != c->device) return cudaErrorInvalidDevice;  // the rank's own GPU
     const kvd_decode_desc r = record_desc(*desc);
     const size_t rec = record_bytes(r);
     char* ws = static_cast<char*>(workspace);

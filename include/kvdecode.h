@@ -14,6 +14,15 @@
  * `solve`); the caller synchronises before reading results. Calls are
  * thread-safe (per-device one-time set-up is guarded); devices with an ordinal
  * of 64 or more are not supported (cudaErrorInvalidDevice).
+ *
+ * Programmatic dependent launch: the head_dim-128 decode kernel lets dependent
+ * grids launch early (griddepcontrol.launch_dependents), and the library
+ * launches its own follow-up kernels (split combine, record exchange) with the
+ * programmatic stream-serialization attribute; they wait (griddepcontrol.wait)
+ * before reading the decode's output. A caller's kernel launched after a
+ * decode WITHOUT that attribute is ordered as usual; one launched WITH it must
+ * itself wait (griddepcontrol.wait / cudaGridDependencySynchronize) before
+ * reading the decode's output.
  */
 #ifndef KVDECODE_H
 #define KVDECODE_H
@@ -345,7 +354,8 @@ cudaError_t kvd_mgpu_p2p_reset(kvd_mgpu_p2p* ctx, cudaStream_t stream);
  * contexts of all `nranks` ranks are made at once, rank r's on device
  * devices[r], and linked by direct peer pointers (peer access is enabled
  * between distinct devices; no IPC, no NCCL). ctxs[r] is used with
- * kvd_mgpu_p2p_seq_split_decode while devices[r] is the current device; the
+ * kvd_mgpu_p2p_seq_split_decode while devices[r] is the current device (any
+ * other current device returns cudaErrorInvalidDevice); the
  * ranks' calls must run concurrently (e.g. one stream per GPU, launched from
  * one thread), since each waits for the others' records (bounded, as above).
  * kvd_mgpu_p2p_reset on a group context needs no communicator: the caller
