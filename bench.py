@@ -399,7 +399,7 @@ class Env:
 
 
 def measure_config(env: Env, cid: int, steps: int, warmup: int, batch: int = 0, paged: int = 0,
-                   qk_int8: bool = False) -> dict:
+                   qk_int8: bool = False, head_shards: bool = False) -> dict:
     """Times configuration `cid` on this process group: device steps replayed
     from CUDA graphs, the end-to-end step through the C ABI with host buffers,
     then the sampled parity check. Frees the configuration's memory on return."""
@@ -417,7 +417,11 @@ def measure_config(env: Env, cid: int, steps: int, warmup: int, batch: int = 0, 
     # Configuration 3 on N > 1 GPUs splits the sequence: rank g holds tokens
     # [g*S/N, (g+1)*S/N) of every head and the ranks merge (m, l, o) records
     # over NVLink (strong scaling). The others shard the batch (weak scaling).
-    seqsplit = cfg.name == "long_context" and world > 1
+    # head_shards: the comparison point for configuration 3 -- rank g owns
+    # H/N heads of every sequence, whole, and nothing crosses NVLink (strong).
+    if head_shards:
+        cfg = dataclasses.replace(cfg, q_heads=cfg.q_heads // world, kv_heads=cfg.kv_heads // world)
+    seqsplit = cfg.name == "long_context" and world > 1 and not head_shards
     exchange = None
     if seqsplit:
         lo, hi = mg.seq_shard(cfg.seq_len, world, rank, align=128)
@@ -437,7 +441,7 @@ def measure_config(env: Env, cid: int, steps: int, warmup: int, batch: int = 0, 
     lens_final = [n + 1 for n in case.lens_host] if cfg.append else (case.lens_host if cfg.ragged else None)
     if not seqsplit:
         nbytes = wl.step_bytes(cfg, lens_final, batch=B)
-        job_bytes = nbytes * world
+        job_bytes = nbytes * world  # weak scaling, or the whole step when the heads are sharded
         if world > 1 and cfg.ragged:  # every rank draws its own lengths: add up the ranks' bytes
             import torch.distributed as dist
 
@@ -588,12 +592,13 @@ def measure_config(env: Env, cid: int, steps: int, warmup: int, batch: int = 0, 
                      f"S={cfg.seq_len}" + (" ragged+append" if cfg.ragged else "")
                      + (" INT8 Q.K mode (KVD_FLAG_QK_INT8)" if qk_int8 else "")
                      + (f" paged cache, {paged}-token blocks in random pool order" if pool else "")),
-        "global_batch": B if seqsplit else B * world, "seq_len": cfg.seq_len,
+        "global_batch": B if (seqsplit or head_shards) else B * world, "seq_len": cfg.seq_len,
         "parallelism": (f"sequence split x{world}, (m, l, o) records exchanged "
                         + ("by peer stores + LSE combine in one kernel" if args.exchange == "p2p"
                            else "by NCCL all-gather + LSE combine")
-                        if seqsplit else f"batch shards x{world}, no comm"),
-        "scaling": "strong" if seqsplit else "weak",
+                        if seqsplit else f"head shards x{world} ({cfg.q_heads} heads per GPU), no comm"
+                        if head_shards else f"batch shards x{world}, no comm"),
+        "scaling": "strong" if (seqsplit or head_shards) else "weak",
         "ms_per_step": ms, "us_per_step": ms * 1e3, "value": job_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
         "gbs_per_gpu": per_gpu_gbs, "pct_of_peak": 100.0 * per_gpu_gbs / peak,
         "bytes_per_step_per_gpu": nbytes,
@@ -708,6 +713,8 @@ def run_ours(args) -> None:
                 configs[str(cid)] = measure_config(env, cid, args.steps, args.warmup)
         # the INT8 Q.K mode on the grouped-query configuration (a looser, stated tolerance)
         configs["5_qk_int8"] = measure_config(env, 5, args.steps, args.warmup, qk_int8=True)
+        if world > 1 and 32 % world == 0:  # configuration 3 sharded by heads: the no-communication comparison
+            configs["3_head_shards"] = measure_config(env, 3, args.steps, args.warmup, head_shards=True)
     peak, peak_kind = measured_peak()
     line = {
         "metric": METRIC, "value": head["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
