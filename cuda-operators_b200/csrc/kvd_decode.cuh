@@ -174,7 +174,16 @@ size_t gqa_workspace_size(const kvd_decode_desc& d);
 struct SplitRecords {
     const float* partials;
     int P;
+    // in: room for tagged records of tagged_P splits per row (gqa_tagged_splits)
+    // and the device word w: the records are tagged *w + 1; tagged == nullptr: none
+    unsigned long long* tagged;
+    int tagged_P;
+    const unsigned int* tag_src;
+    bool tagged_used;  // out: the decode wrote tagged records
 };
+// Split count per row of the tensor-core decode when it may write tagged
+// records for `d` (dense batch, group <= 4, head_dim 128), else 0.
+int gqa_tagged_splits(const kvd_decode_desc& d);
 cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const void* Q, const int8_t* K, const int8_t* V,
                           const float* ks, const float* vs, void* out, void* ws, size_t ws_bytes,
                           cudaStream_t st, int* launches, const PagedView* pv = nullptr,

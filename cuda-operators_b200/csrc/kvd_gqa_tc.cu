@@ -73,7 +73,18 @@ struct GqaParams {
     int32_t* lens_rw;
     unsigned int* done_ctas;
     int len_add;
+    // Tagged split records for a consumer that runs beside this grid (the
+    // multi-GPU exchange), dense batches only: record (row, split) of D+4 words
+    // at tagged + ((b * Hq + hq) * P + split) * (D + 4), each word {value bits,
+    // tag << 32} written with one 8-byte store, so a reader that sees the tag
+    // sees the value and no fence or count is needed. tag = *tag_src + 1, read
+    // by every CTA before it allows its programmatic dependents to launch.
+    // Compiled for groups up to kTagMaxGroup only (the larger groups' kernels
+    // are at their register limit). nullptr: float records.
+    unsigned long long* tagged;
+    const unsigned int* tag_src;
 };
+constexpr int kTagMaxGroup = 4;
 
 template <int G, int NK_, int NV_, int QM_>
 struct GqaCfg {
@@ -117,6 +128,7 @@ struct GqaCfg {
     static constexpr int NBAR = B_APPEND + 1;
     static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;  // TMEM address, then the fused-append list count
     static constexpr int OFF_APPENDED = OFF_TMEM + 8;
+    static constexpr int OFF_TAG = OFF_TMEM + 12;  // tagged records: the call's tag
     static constexpr int SMEM_USED = OFF_TMEM + 16;
     static constexpr int SMEM_BYTES = SMEM_USED + 1024;           // slack to align the base to 1024
     static_assert(G >= 1 && G <= 16 && G % NWG == 0 && CPW % 16 == 0, "group size");
@@ -196,6 +208,11 @@ __device__ __forceinline__ GItem gqa_item(const GqaParams& p, int it) {
 __device__ __forceinline__ int next_item(const GqaParams& p, int it) {
     while (it < p.n_items && gqa_item(p, it).ntiles == 0) it += p.grid;
     return it;
+}
+
+__device__ __forceinline__ void st_tagged_gpu(unsigned long long* p, float v, unsigned int tag) {
+    const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
 struct __align__(16) GMeta {
@@ -725,7 +742,8 @@ __device__ __forceinline__ bool gqa_pv_epi(const GqaParams& p, uint8_t* smem, ui
                                            const float (&mA)[GqaCfg<G, NK, NV, QM>::HPW],
                                            const int (&FA)[GqaCfg<G, NK, NV, QM>::HPW],
                                            const float (&LA)[GqaCfg<G, NK, NV, QM>::HPW],
-                                           float (&o)[GqaCfg<G, NK, NV, QM>::HPW], float (&mpv)[GqaCfg<G, NK, NV, QM>::HPW]) {
+                                           float (&o)[GqaCfg<G, NK, NV, QM>::HPW], float (&mpv)[GqaCfg<G, NK, NV, QM>::HPW],
+                                           unsigned int tag) {
     using C = GqaCfg<G, NK, NV, QM>;
     constexpr int NP = C::NP, HPW = C::HPW, CPW = C::CPW;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -762,6 +780,18 @@ __device__ __forceinline__ bool gqa_pv_epi(const GqaParams& p, uint8_t* smem, ui
         for (int h = 0; h < HPW; ++h) {
             const int hq = I.hk * G + wg * HPW + h;
             const int64_t ro = I.b * p.o_sb + static_cast<int64_t>(hq) * p.o_sh;
+            if constexpr (G <= kTagMaxGroup) {
+                if (p.tagged) {  // every row of a dense batch, P >= 1 records
+                    unsigned long long* rec =
+                        p.tagged + ((static_cast<int64_t>(I.b) * p.Hq + hq) * p.P + I.split) * (C::D + 4);
+                    if (r == 0) {
+                        st_tagged_gpu(rec, mA[h], tag);
+                        st_tagged_gpu(rec + 1, LA[h], tag);
+                    }
+                    st_tagged_gpu(rec + 4 + r, o[h], tag);
+                    continue;
+                }
+            }
             if (!records) {
                 store_out(p.out, ro + r, LA[h] > 0.f ? o[h] / LA[h] : 0.f, p.flags);
             } else {
@@ -796,6 +826,7 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
     uint32_t use = 0;
 
     if (p.k_new) fused_append_rows<G, NK, NV, QM>(p, smem);
+    const unsigned int tag = *reinterpret_cast<const unsigned int*>(smem + C::OFF_TAG);  // tagged records
 
     // Zero this warpgroup's rows of both query-limb buffers (pad rows stay
     // zero), then item 0's limbs (its reduction orders the zeroing first).
@@ -863,7 +894,7 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
             // (thread r = output dim r) while the other warps catch up, then
             // collect the warpgroup maxima.
             epi_reduce_post<HPW + 1, true>(rv, red, red_bar, use);
-            if (A.i >= 0 && !gqa_pv_epi<G, NK, NV, QM>(p, smem, tmem, A, mA, FA, LA, o, mpv)) return;
+            if (A.i >= 0 && !gqa_pv_epi<G, NK, NV, QM>(p, smem, tmem, A, mA, FA, LA, o, mpv, tag)) return;
             if (!epi_reduce_finish<HPW + 1, true>(rv, red, red_bar, use)) return;
             const float vsmax = rv[HPW];
             // ---- online softmax (base 2, lazy max) and the weight limbs
@@ -918,7 +949,7 @@ __device__ __forceinline__ void gqa_epilogue(const GqaParams& p, uint8_t* smem, 
             A.flags = mt.flags;
         }
     }
-    if (A.i >= 0) gqa_pv_epi<G, NK, NV, QM>(p, smem, tmem, A, mA, FA, LA, o, mpv);
+    if (A.i >= 0) gqa_pv_epi<G, NK, NV, QM>(p, smem, tmem, A, mA, FA, LA, o, mpv, tag);
 }
 
 // Fused append, end of a CTA: once every thread of the CTA is past its last
@@ -951,9 +982,14 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV, QM>::THREADS, MINB) gqa_tc_k
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     // A follow-up kernel launched as a programmatic dependent (the split combine,
     // the multi-GPU record exchange) may be scheduled onto SMs as this grid's
-    // CTAs retire; it waits for this grid's completion before reading its output.
-    allow_dependents();
-    if (next_item(p, blockIdx.x) >= p.n_items) {  // no (non-empty) item for this CTA
+    // CTAs retire; it waits for this grid's completion before reading its
+    // output. With tagged records the dependent (the exchange) reads them while
+    // this grid runs and moves the tag word on when it ends: every CTA reads
+    // the tag first and allows the dependents to launch only after that.
+    bool tagged = false;
+    if constexpr (G <= kTagMaxGroup) tagged = p.tagged != nullptr;
+    if (!tagged) allow_dependents();
+    if (next_item(p, blockIdx.x) >= p.n_items) {  // no (non-empty) item for this CTA (exiting allows the dependents)
         if (p.k_new) fused_append_finish(p);
         return;
     }
@@ -962,6 +998,8 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV, QM>::THREADS, MINB) gqa_tc_k
     uint64_t* done = bars + C::B_DONE;
     uint64_t* drain = bars + C::B_DRAIN;
     if (threadIdx.x == 0) {
+        unsigned int tag = 0;
+        if (tagged) asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(tag) : "l"(p.tag_src) : "memory");
         for (int s = 0; s < NK; ++s) {
             mbar_init(&bars[C::B_KFULL + s], 1);       // producer arrive + transaction bytes
             mbar_init(&bars[C::B_KEMPTY + s], 1);      // QK commit
@@ -983,10 +1021,12 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV, QM>::THREADS, MINB) gqa_tc_k
         mbar_init(drain, 1);
         *reinterpret_cast<int*>(smem + C::OFF_APPENDED) = 0;
         mbar_init(&bars[C::B_APPEND], EW);  // every epilogue warp, after its share of the fused append
+        if (tagged) *reinterpret_cast<unsigned int*>(smem + C::OFF_TAG) = tag + 1;
         fence_mbar_init();
     }
     if (warp == EW + 1) tmem_alloc(reinterpret_cast<uint32_t*>(smem + C::OFF_TMEM), C::TMEM_COLS);
     __syncthreads();
+    if (tagged) allow_dependents();  // every CTA of this grid has read the tag
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + C::OFF_TMEM);
     if (warp == EW) {
@@ -1235,6 +1275,11 @@ GqaPlan plan_gqa(const kvd_decode_desc& d, size_t ws_limit) {
 }
 }  // namespace
 
+int gqa_tagged_splits(const kvd_decode_desc& d) {
+    if (!gqa_path_ok(d) || d.seq_lens || d.num_q_heads / d.num_kv_heads > kTagMaxGroup) return 0;
+    return plan_gqa(d, ~size_t(0)).P;
+}
+
 bool gqa_fused_append_ok(const kvd_decode_desc& d, size_t ws_bytes) {
     return gqa_path_ok(d) && d.seq_lens && plan_gqa(d, ws_bytes).order_bytes > 0;
 }
@@ -1285,6 +1330,13 @@ cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const void* Q, const int8_t*
     const float scale = d.softmax_scale > 0.f ? d.softmax_scale : 1.0f / sqrtf(static_cast<float>(d.head_dim));
     p.qscale = scale * 1.4426950408889634f;
     p.flags = d.flags;
+    // Tagged records: dense batches only, where every item is non-empty
+    // (max_seq_len >= 1) and every row gets exactly P records.
+    if (keep_splits && keep_splits->tagged && keep_splits->tagged_P == g.P && !d.seq_lens && !pv && !av &&
+        G <= kTagMaxGroup) {
+        p.tagged = keep_splits->tagged;
+        p.tag_src = keep_splits->tag_src;
+    }
     unsigned int* done_ctas = nullptr;
     if (av) {
         p.k_new = av->k_new; p.v_new = av->v_new; p.new_sb = av->new_sb; p.new_sh = av->new_sh;
@@ -1319,6 +1371,7 @@ cudaError_t launch_gqa_tc(const kvd_decode_desc& d, const void* Q, const int8_t*
     if (keep_splits) {  // the caller merges the split records itself (dense batches only)
         keep_splits->partials = g.P > 1 && !d.seq_lens ? p.partials : nullptr;
         keep_splits->P = g.P > 1 && !d.seq_lens ? g.P : 1;
+        keep_splits->tagged_used = p.tagged != nullptr;
         if (g.P == 1 || !d.seq_lens) return cudaSuccess;
     }
     if (g.P > 1) {

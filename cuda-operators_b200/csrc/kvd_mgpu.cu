@@ -141,177 +141,351 @@ extern "C" cudaError_t kvd_mgpu_seq_split_decode(const kvd_decode_desc* desc, co
 }
 
 // ---------------------------------------------------------------- peer exchange
-// The sequence split without NCCL on the hot path: after the local decode, ONE
-// kernel merges this rank's split records of each row, pushes the merged
-// record straight into every rank's gather buffer over NVLink (peer stores
-// through CUDA IPC mappings), raises a flag per (rank, CTA) in every peer's
-// memory, waits (bounded) for all ranks' flags and merges the gathered records
-// into output rows. NCCL is used at set-up (to swap the IPC handles) and by
-// the collective reset only.
+// The sequence split without NCCL on the hot path: ONE kernel, launched as a
+// programmatic dependent of the local decode, merges this rank's split records
+// of each row, pushes the merged record straight into every rank's gather
+// buffer over NVLink (peer stores through CUDA IPC mappings), waits (bounded)
+// for every rank's record of its rows and merges them into output rows. NCCL
+// is used at set-up (to swap the IPC handles) and by the collective reset only.
 //
-// Persistent grid: the kernel runs at most as many CTAs as fit on the GPU at
-// once, each looping over row blocks (first pushing all of them, then waiting).
-// Every CTA therefore runs and pushes before any CTA of this rank has to wait,
-// so no CTA waits on a peer CTA that cannot be scheduled, whatever the batch.
+// Tagged words: records cross NVLink as 8-byte words {value bits, epoch << 32}.
+// An aligned 8-byte store is single-copy atomic, so a reader that sees the
+// current epoch in a word also sees the value stored with it: no fence and no
+// flag has to follow a push. The tensor-core decode (dense batch, group <= 4)
+// writes its split records in the same form, so the exchange CTAs, resident
+// beside the decode's, merge and push each row as soon as its records are
+// there, during the decode's last items. Otherwise the decode writes float
+// records and the kernel first waits (griddepcontrol.wait) for the whole
+// decode grid.
 //
-// Epochs: CTA c keeps its own call count in local device memory; every rank
-// runs the same calls, so CTA c of every rank uses the same epoch e and writes
-// buffer parity e & 1. A rank can be at most one epoch ahead of a peer (its
-// step e + 1 needs the peer's step-e flags, raised after the peer finished
-// step e - 1), so two parities never collide. A rank that misses a call breaks
-// that agreement: the others time out, and kvd_mgpu_p2p_reset restores it.
+// Epochs: CTA c keeps its own call count epochs[c] in local device memory and
+// uses e = epochs[c] + 1, storing e back when it ends. Every rank makes the
+// same calls, so CTA c of every rank uses the same e. The tagged decode tags
+// its records with epochs[0] + 1, read by each of its CTAs before it allows
+// this kernel to launch, so before CTA 0 can move epochs[0] on. Gather buffers
+// alternate by parity e & 1: a rank can be at most one call ahead of a peer
+// (its call e + 1 needs the peer's records of call e, pushed after the peer
+// finished call e - 1), so two parities never collide. A rank that misses a
+// call breaks the agreement: the others time out, and kvd_mgpu_p2p_reset
+// restores it.
+//
+// Persistent grid: at most as many CTAs as fit on an idle GPU, each looping
+// over its rows (first merging and pushing all of them, then waiting for the
+// peers'). A programmatic dependent starts only after every CTA of the decode
+// has started, so the decode runs to its end whatever the exchange waits for;
+// and every exchange CTA pushes all its rows before it waits for a peer.
 namespace kvd {
 namespace {
 
-constexpr int kP2PRows = 1;         // record rows per block of the exchange kernel
-constexpr int kP2PThreads = 128;
+constexpr int kP2PThreads = 128;  // 4 warps
+constexpr int kP2PWarps = kP2PThreads / 32;
 constexpr int kMaxRanks = 8;
-constexpr int kMaxMerge = 256;      // records merged per row (split count cap of the planner)
+constexpr int kMaxMerge = 256;  // records merged per row (split count cap of the planner)
+constexpr int kMaxDim = 256;    // head_dim bound of the exchange
+constexpr int kRecs = 4;        // records a thread holds at once (x 4 dimensions = 16 tagged words)
 
 struct P2PPeers {
-    float* gather[kMaxRanks];        // rank p's gather buffer [2][nranks][rows][D+4]
-    unsigned int* flags[kMaxRanks];  // rank p's flags [nranks][ctas]
+    unsigned long long* gather[kMaxRanks];  // rank p's gather buffer [2][nranks][rows][D+4] tagged words
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_tagged(unsigned long long* p, float v, unsigned int e) {
+    const unsigned long long w = (static_cast<unsigned long long>(e) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
-__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
-    unsigned int v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
 }
 
-// Log-sum-exp weights of the n records of one row (record k at first +
-// k*stride, n <= kMaxMerge), computed by the whole CTA: the records' maxima
-// and weights wk[k] = 2^(m_k - M) are each computed once, spread over the
-// threads and kept in shared memory, so the per-dimension sums that follow
-// (sum_k wk[k] * o_k[d]) run over independent loads. Every thread returns M
-// and L = sum_k wk[k] * l_k. Ends with a barrier: red is free again, wk holds
-// the weights until the caller's next barrier.
-template <bool CACHED>
-__device__ __forceinline__ void merge_weights(const float* first, int n, size_t stride, float* wk, float* red,
-                                              float& M, float& L) {
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
-    auto ld = [](const float* x) { return CACHED ? __ldcg(x) : __ldg(x); };
-    float m = -INFINITY;
-    for (int k = t; k < n; k += blockDim.x) m = fmaxf(m, ld(first + k * stride));
-    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    if (lane == 0) red[warp] = m;
+// Two consecutive tagged words (p 16-byte aligned); each is single-copy atomic.
+__device__ __forceinline__ void ld_tagged2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+__device__ __forceinline__ bool tag_is(unsigned long long w, unsigned int e) {
+    return static_cast<unsigned int>(w >> 32) == e;
+}
+
+// One more poll of a word that does not carry the epoch yet: sleeps ns
+// (doubled up to 512 ns for the next poll). t0 is the start of the first wait
+// (0 before); returns false past kWaitTimeoutNs.
+__device__ __forceinline__ bool backoff(uint64_t& t0, unsigned int& ns) {
+    const uint64_t now = globaltimer_ns();
+    if (t0 == 0) {
+        t0 = now;
+    } else if (now - t0 > kWaitTimeoutNs) {
+        return false;
+    }
+    __nanosleep(ns);
+    if (ns < 512) ns *= 2;
+    return true;
+}
+
+// Waits (bounded) until the tagged word w, loaded from p, carries epoch e.
+__device__ __forceinline__ bool wait_word(const unsigned long long* p, unsigned int e, unsigned long long& w,
+                                          uint64_t& t0) {
+    unsigned int ns = 64;
+    while (!tag_is(w, e)) {
+        if (!backoff(t0, ns)) return false;
+        w = ld_tagged(p);
+    }
+    return true;
+}
+
+struct MergeSmem {
+    float ms[kMaxMerge], ls[kMaxMerge], wk[kMaxMerge];
+    float part[kP2PWarps][kMaxDim];
+    float red[kP2PWarps];
+};
+
+// One thread's share of a row of n tagged records (record k at first +
+// k * stride: m, l, 2 unused, o[D]): with_ml, m and l of records t, t + 128,
+// ... into sm.ms / sm.ls; and o[4g .. 4g+3] (g = dimension group) of the
+// records k0 + warp + 4j (j < kRecs) into o[j]. All loads are issued before
+// the first check. wait == false: returns whether every word carries epoch e.
+// wait == true: a word that does not is polled alone until it does (bounded);
+// false on timeout.
+__device__ __forceinline__ bool load_share(const unsigned long long* first, int n, size_t stride, int g, int k0,
+                                           bool with_ml, unsigned int e, MergeSmem& sm, float (&o)[kRecs][4],
+                                           bool wait, uint64_t& t0) {
+    const int t = threadIdx.x, warp = t >> 5;
+    unsigned long long w[kRecs][4];
+#pragma unroll
+    for (int j = 0; j < kRecs; ++j) {
+        const int k = k0 + warp + kP2PWarps * j;
+        if (k < n) {
+            const unsigned long long* q = first + k * stride + 4 + 4 * g;
+            ld_tagged2(q, w[j][0], w[j][1]);
+            ld_tagged2(q + 2, w[j][2], w[j][3]);
+        }
+    }
+    bool all = true;
+    if (with_ml)
+        for (int k = t; k < n; k += blockDim.x) {
+            unsigned long long m, l;
+            ld_tagged2(first + k * stride, m, l);
+            if (wait) {
+                if (!wait_word(first + k * stride, e, m, t0) || !wait_word(first + k * stride + 1, e, l, t0))
+                    return false;
+            } else if (!tag_is(m, e) || !tag_is(l, e)) {
+                all = false;
+            }
+            sm.ms[k] = __uint_as_float(static_cast<unsigned int>(m));
+            sm.ls[k] = __uint_as_float(static_cast<unsigned int>(l));
+        }
+#pragma unroll
+    for (int j = 0; j < kRecs; ++j) {
+        const int k = k0 + warp + kP2PWarps * j;
+        if (k < n) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (!tag_is(w[j][i], e)) {
+                    if (!wait) {
+                        all = false;
+                        continue;
+                    }
+                    if (!wait_word(first + k * stride + 4 + 4 * g + i, e, w[j][i], t0)) return false;
+                }
+                o[j][i] = __uint_as_float(static_cast<unsigned int>(w[j][i]));
+            }
+        }
+    }
+    return all;
+}
+
+// Log-sum-exp merge of the n tagged records of one row (record k at first +
+// k * stride, D+4 words; n <= kMaxMerge, D <= kMaxDim, D % 4 == 0) by the
+// whole CTA, once every word it uses carries epoch e. Lane l of each warp
+// takes dimensions 4l .. 4l+3 (and 128 higher, for D > 128); warp w takes
+// records w, w + 4, ..., kRecs at a time, so up to 16 records cost one round
+// of loads. emit(d, O, L) receives each dimension's unnormalised sum
+// O = sum_k w_k o_k[d], w_k = 2^(m_k - M), with L = sum_k w_k l_k; M and L
+// are also returned. When a first round finds words missing, one thread polls
+// (with backoff) until the first word of every record carries e, and the CTA
+// loads again, so a waiting CTA adds one poller, not one a thread. A thread
+// reads a word again only after it has seen it tagged with e. Returns false
+// (on every thread) when a wait ran out.
+template <class Emit>
+__device__ __forceinline__ bool merge_tagged(const unsigned long long* first, int n, size_t stride, int D,
+                                             unsigned int e, MergeSmem& sm, float& M, float& L, Emit emit) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int groups = D >> 2;
+    float o[kRecs][4];
+    uint64_t t0 = 0;
+    const int g0 = lane < groups ? lane : 0;  // this lane's first dimension group
+    bool ok = load_share(first, n, stride, g0, 0, true, e, sm, o, false, t0);
+    if (!__syncthreads_and(ok)) {
+        ok = true;
+        if (t == 0) {
+            unsigned int ns = 64;
+            for (int k = 0; k < n && ok; ++k)
+                while (!tag_is(ld_tagged(first + k * stride), e))
+                    if (!backoff(t0, ns)) {
+                        ok = false;
+                        break;
+                    }
+        }
+        if (!__syncthreads_and(ok)) return false;
+        ok = load_share(first, n, stride, g0, 0, true, e, sm, o, true, t0);
+        if (!__syncthreads_and(ok)) return false;
+    }
+    // weights: every thread from sm.ms / sm.ls (few records), or block-wide; kept in sm.wk
+    if (n <= 32) {
+        M = -INFINITY;
+        for (int k = 0; k < n; ++k) M = fmaxf(M, sm.ms[k]);
+        L = 0.f;
+        for (int k = 0; k < n; ++k) {
+            const float f = M == -INFINITY ? 0.f : exp2f(sm.ms[k] - M);
+            if (k == t) sm.wk[k] = f;
+            L = fmaf(f, sm.ls[k], L);
+        }
+        __syncthreads();  // sm.wk is complete
+    } else {
+        float m = -INFINITY;
+        for (int k = t; k < n; k += blockDim.x) m = fmaxf(m, sm.ms[k]);
+        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        if (lane == 0) sm.red[warp] = m;
+        __syncthreads();
+        M = sm.red[0];
+        for (int w = 1; w < kP2PWarps; ++w) M = fmaxf(M, sm.red[w]);
+        float l = 0.f;
+        for (int k = t; k < n; k += blockDim.x) {
+            const float f = M == -INFINITY ? 0.f : exp2f(sm.ms[k] - M);
+            sm.wk[k] = f;
+            l = fmaf(f, sm.ls[k], l);
+        }
+        for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+        __syncthreads();  // every thread has read the maxima in red
+        if (lane == 0) sm.red[warp] = l;
+        __syncthreads();  // the sums are in red and the weights in wk
+        L = 0.f;
+        for (int w = 0; w < kP2PWarps; ++w) L += sm.red[w];
+    }
+    // this warp's partial sums over its records, dimension group by group
+    for (int g = lane; g < groups; g += 32) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int k0 = 0; k0 < n && ok; k0 += kP2PWarps * kRecs) {
+            // records not held from the first round: load again (waiting where a tag is not there yet)
+            if ((g != lane || k0 > 0) && !load_share(first, n, stride, g, k0, false, e, sm, o, true, t0)) {
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int j = 0; j < kRecs; ++j) {
+                const int k = k0 + warp + kP2PWarps * j;
+                if (k < n) {
+                    const float f = sm.wk[k];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) acc[i] = fmaf(f, o[j][i], acc[i]);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sm.part[warp][4 * g + i] = acc[i];
+    }
+    if (!__syncthreads_and(ok)) return false;
+    for (int d = t; d < D; d += blockDim.x) {
+        float O = 0.f;
+#pragma unroll
+        for (int w = 0; w < kP2PWarps; ++w) O += sm.part[w][d];
+        emit(d, O, L);
+    }
+    __syncthreads();  // sm is rewritten by the next row
+    return true;
+}
+
+// The same merge over n float records written by a decode grid that has
+// completed (record k at first + k * stride).
+template <class Emit>
+__device__ __forceinline__ void merge_float(const float* first, int n, size_t stride, int D, MergeSmem& sm, float& M,
+                                            float& L, Emit emit) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    for (int k = t; k < n; k += blockDim.x) {
+        sm.ms[k] = __ldcg(first + k * stride);
+        sm.ls[k] = __ldcg(first + k * stride + 1);
+    }
     __syncthreads();
-    M = red[0];
-    for (int w = 1; w < nw; ++w) M = fmaxf(M, red[w]);
+    float m = -INFINITY;
+    for (int k = t; k < n; k += blockDim.x) m = fmaxf(m, sm.ms[k]);
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (lane == 0) sm.red[warp] = m;
+    __syncthreads();
+    M = sm.red[0];
+    for (int w = 1; w < kP2PWarps; ++w) M = fmaxf(M, sm.red[w]);
     float l = 0.f;
     for (int k = t; k < n; k += blockDim.x) {
-        const float f = M == -INFINITY ? 0.f : exp2f(ld(first + k * stride) - M);
-        wk[k] = f;
-        l = fmaf(f, ld(first + k * stride + 1), l);
+        const float f = M == -INFINITY ? 0.f : exp2f(sm.ms[k] - M);
+        sm.wk[k] = f;
+        l = fmaf(f, sm.ls[k], l);
     }
     for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-    __syncthreads();  // every thread has read the maxima in red
-    if (lane == 0) red[warp] = l;
-    __syncthreads();  // the sums are in red and the weights in wk
-    L = 0.f;
-    for (int w = 0; w < nw; ++w) L += red[w];
-    __syncthreads();  // red is reused by the next call
-}
-
-template <bool CACHED>
-__device__ __forceinline__ float merged_dim(const float* first, int n, size_t stride, const float* wk, int d) {
-    float acc = 0.f;
-#pragma unroll 4
-    for (int k = 0; k < n; ++k) acc = fmaf(wk[k], CACHED ? __ldcg(first + k * stride + 4 + d) : __ldg(first + k * stride + 4 + d), acc);
-    return acc;
-}
-
-// src: this rank's records, P consecutive records of D+4 floats per row (the
-// decode's split records; P == 1: one record per row).
-__global__ void __launch_bounds__(kP2PThreads) p2p_exchange_combine_kernel(
-    const float* __restrict__ src, int P, const P2PPeers peers, unsigned int* epochs, int nranks, int rank,
-    int rows, int D, int rows_per_b, void* out, int64_t o_sb, int64_t o_sh, uint32_t flags) {
-    const int c = blockIdx.x, ctas = gridDim.x;
-    const int rs = D + 4;
-    const int nblk = (rows + kP2PRows - 1) / kP2PRows;
-    __shared__ unsigned int e_sh;
-    __shared__ int ok_sh;
-    __shared__ float wk[kMaxMerge];
-    __shared__ float red[kP2PThreads / 32];
-    grid_dependency_wait();  // launched as a programmatic dependent of the local decode: its records are complete
-    if (threadIdx.x == 0) e_sh = ++epochs[c];
     __syncthreads();
-    const unsigned int e = e_sh;
+    if (lane == 0) sm.red[warp] = l;
+    __syncthreads();
+    L = 0.f;
+    for (int w = 0; w < kP2PWarps; ++w) L += sm.red[w];
+    for (int d = t; d < D; d += blockDim.x) {
+        float O = 0.f;
+#pragma unroll 8
+        for (int k = 0; k < n; ++k) O = fmaf(sm.wk[k], __ldcg(first + k * stride + 4 + d), O);
+        emit(d, O, L);
+    }
+    __syncthreads();  // sm is rewritten by the next row
+}
+
+// Records of this rank: tagged (P per row, from a tagged decode that may still
+// be running) or float (src, P per row, from a completed decode grid).
+// At most 152 registers a thread (launched with kP2PThreads threads): a CTA
+// then fits on an SM beside two CTAs of the group-1 decode (120 registers a
+// thread after allocation rounding) and runs while they do.
+__global__ void __maxnreg__(152) p2p_exchange_combine_kernel(
+    const float* __restrict__ src, const unsigned long long* tagged, int P, const __grid_constant__ P2PPeers peers,
+    unsigned int* epochs, int nranks, int rank, int rows, int D, int rows_per_b, void* out, int64_t o_sb,
+    int64_t o_sh, uint32_t flags) {
+    const int c = blockIdx.x, ctas = gridDim.x, t = threadIdx.x;
+    const int rs = D + 4;
+    __shared__ MergeSmem sm;
+    if (!tagged) grid_dependency_wait();  // launched as a programmatic dependent: the float records are complete
+    const unsigned int e = *reinterpret_cast<volatile unsigned int*>(epochs + c) + 1;
     const int par = static_cast<int>(e & 1u);
     const size_t slab = static_cast<size_t>(rows) * rs;  // one rank's records
-    // 1. merge this rank's split records of every row of this CTA's blocks and
-    //    push the merged record into every rank's gather buffer
-    for (int blk = c; blk < nblk; blk += ctas) {
-        const int r1 = min(rows, (blk + 1) * kP2PRows);
-        for (int r = blk * kP2PRows; r < r1; ++r) {
-            const float* rec = src + static_cast<size_t>(r) * P * rs;
-            const size_t dst_off = (static_cast<size_t>(par) * nranks + rank) * slab + static_cast<size_t>(r) * rs;
-            if (P == 1) {
-                for (int i = threadIdx.x; i < rs / 4; i += blockDim.x) {
-                    const float4 v = __ldg(reinterpret_cast<const float4*>(rec) + i);
-                    for (int p = 0; p < nranks; ++p) reinterpret_cast<float4*>(peers.gather[p] + dst_off)[i] = v;
-                }
-                continue;
+    // 1. per row: merge this rank's split records and push the merged record
+    //    into every rank's gather buffer
+    for (int r = c; r < rows; r += ctas) {
+        const size_t dst_off = (static_cast<size_t>(par) * nranks + rank) * slab + static_cast<size_t>(r) * rs;
+        auto push = [&](int d, float O, float) {
+            for (int p = 0; p < nranks; ++p) st_tagged(peers.gather[p] + dst_off + 4 + d, O, e);
+        };
+        float M, L;
+        if (tagged) {
+            if (!merge_tagged(tagged + static_cast<size_t>(r) * P * rs, P, rs, D, e, sm, M, L, push)) {
+                if (t == 0) record_status(KVD_STATUS_WAIT_TIMEOUT);  // the decode did not finish this row
+                return;
             }
-            float M, L;
-            merge_weights<false>(rec, P, rs, wk, red, M, L);
-            for (int d = threadIdx.x; d < D; d += blockDim.x) {
-                const float O = merged_dim<false>(rec, P, rs, wk, d);
-                for (int p = 0; p < nranks; ++p) {
-                    float* dst = peers.gather[p] + dst_off;
-                    dst[4 + d] = O;
-                    if (d == 0) { dst[0] = M; dst[1] = L; }
-                }
-            }
-            __syncthreads();  // wk is rewritten by the next row
+        } else {
+            merge_float(src + static_cast<size_t>(r) * P * rs, P, rs, D, sm, M, L, push);
+        }
+        if (t < nranks) {  // the row's M and L, one rank per thread
+            st_tagged(peers.gather[t] + dst_off, M, e);
+            st_tagged(peers.gather[t] + dst_off + 1, L, e);
         }
     }
-    __syncthreads();
-    // 2. publish: one release store per rank, ordered after every thread's stores
-    if (threadIdx.x < nranks) {
-        __threadfence_system();
-        st_release_sys(peers.flags[threadIdx.x] + static_cast<size_t>(rank) * ctas + c, e);
-    }
-    // 3. wait for every rank's flag of this CTA and epoch (bounded)
-    if (threadIdx.x == 0) ok_sh = 1;
-    __syncthreads();
-    if (threadIdx.x < nranks) {
-        const unsigned int* f = peers.flags[rank] + static_cast<size_t>(threadIdx.x) * ctas + c;
-        if (static_cast<int>(ld_acquire_sys(f) - e) < 0) {
-            const uint64_t t0 = globaltimer_ns();
-            while (static_cast<int>(ld_acquire_sys(f) - e) < 0) {
-                __nanosleep(256);
-                if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
-                    record_status(KVD_STATUS_WAIT_TIMEOUT);
-                    ok_sh = 0;
-                    break;
-                }
-            }
+    // 2. per row: every rank's record (bounded waits on the tags), merged into
+    //    the output row
+    const unsigned long long* mine = peers.gather[rank] + static_cast<size_t>(par) * nranks * slab;
+    for (int r = c; r < rows; r += ctas) {
+        const int b = r / rows_per_b, h = r - b * rows_per_b;
+        const int64_t ro = b * o_sb + static_cast<int64_t>(h) * o_sh;
+        float M, L;
+        auto write = [&](int d, float O, float Lr) { store_out(out, ro + d, Lr > 0.f ? O / Lr : 0.f, flags); };
+        if (!merge_tagged(mine + static_cast<size_t>(r) * rs, nranks, slab, D, e, sm, M, L, write)) {
+            if (t == 0) record_status(KVD_STATUS_WAIT_TIMEOUT);  // a rank missed this call: rows stay unwritten
+            return;
         }
     }
-    __syncthreads();
-    if (!ok_sh) return;  // a rank missed this call: these rows stay unwritten (the status says so)
-    // 4. log-sum-exp merge of this CTA's rows (records read from L2: peers wrote them)
-    const float* mine = peers.gather[rank] + static_cast<size_t>(par) * nranks * slab;
-    for (int blk = c; blk < nblk; blk += ctas) {
-        const int r1 = min(rows, (blk + 1) * kP2PRows);
-        for (int r = blk * kP2PRows; r < r1; ++r) {
-            const float* first = mine + static_cast<size_t>(r) * rs;
-            float M, L;
-            merge_weights<true>(first, nranks, slab, wk, red, M, L);
-            const int b = r / rows_per_b, h = r - b * rows_per_b;
-            const int64_t ro = b * o_sb + static_cast<int64_t>(h) * o_sh;
-            for (int d = threadIdx.x; d < D; d += blockDim.x) {
-                const float O = merged_dim<true>(first, nranks, slab, wk, d);
-                store_out(out, ro + d, L > 0.f ? O / L : 0.f, flags);
-            }
-            __syncthreads();  // wk is rewritten by the next row
-        }
-    }
+    if (t == 0) epochs[c] = e;  // this CTA's call is complete
 }
 
 }  // namespace
@@ -322,8 +496,8 @@ struct kvd_mgpu_p2p {
     int device;               // the rank's device
     size_t slab_floats, region_bytes;
     void* comm;               // the communicator given at creation (reset barriers); nullptr in a group
-    void* region;             // this rank's gather buffer + flags (IPC-exported)
-    unsigned int* epochs;     // local per-CTA epoch counters
+    void* region;             // this rank's gather buffer of tagged words (IPC-exported)
+    unsigned int* epochs;     // [ctas] the exchange CTAs' call counts (local)
     int* barrier_buf;         // [nranks + 1] ints for the reset's NCCL barriers
     kvd::P2PPeers peers;
     void* opened[kvd::kMaxRanks];  // IPC mappings of the peers' regions
@@ -332,7 +506,7 @@ struct kvd_mgpu_p2p {
 extern "C" cudaError_t kvd_mgpu_p2p_create(kvd_mgpu_p2p** out, int batch, int num_q_heads, int head_dim, void* comm,
                                            int nranks, int rank) {
     using namespace kvd;
-    if (!out || !comm || batch < 1 || num_q_heads < 1 || head_dim < 1 || (head_dim & 3) != 0 || nranks < 1 ||
+    if (!out || !comm || batch < 1 || num_q_heads < 1 || head_dim < 1 || head_dim > kMaxDim || (head_dim & 3) != 0 || nranks < 1 ||
         nranks > kMaxRanks || rank < 0 || rank >= nranks)
         return cudaErrorInvalidValue;
     const NcclApi& api = nccl();
@@ -349,12 +523,9 @@ extern "C" cudaError_t kvd_mgpu_p2p_create(kvd_mgpu_p2p** out, int batch, int nu
     c->comm = comm;
     cudaGetDevice(&c->device);
     c->rows = batch * num_q_heads;
-    const int64_t nblk = (c->rows + kP2PRows - 1) / kP2PRows;
-    c->ctas = static_cast<int>(nblk < resident ? nblk : resident);
+    c->ctas = static_cast<int>(c->rows < resident ? c->rows : resident);
     c->slab_floats = static_cast<size_t>(c->rows) * (head_dim + 4);
-    const size_t gather_bytes = align256(2 * static_cast<size_t>(nranks) * c->slab_floats * sizeof(float));
-    const size_t flag_bytes = align256(static_cast<size_t>(nranks) * c->ctas * sizeof(unsigned int));
-    c->region_bytes = gather_bytes + flag_bytes;
+    c->region_bytes = align256(2 * static_cast<size_t>(nranks) * c->slab_floats * sizeof(unsigned long long));
     e = cudaMalloc(&c->region, c->region_bytes);
     if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c->epochs), c->ctas * sizeof(unsigned int));
     if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c->barrier_buf), (nranks + 1) * sizeof(int));
@@ -380,8 +551,7 @@ extern "C" cudaError_t kvd_mgpu_p2p_create(kvd_mgpu_p2p** out, int batch, int nu
             e = cudaIpcOpenMemHandle(&base, all[p], cudaIpcMemLazyEnablePeerAccess);
             c->opened[p] = e == cudaSuccess ? base : nullptr;
         }
-        c->peers.gather[p] = static_cast<float*>(base);
-        c->peers.flags[p] = reinterpret_cast<unsigned int*>(static_cast<char*>(base) + gather_bytes);
+        c->peers.gather[p] = static_cast<unsigned long long*>(base);
     }
     if (e != cudaSuccess) {
         kvd_mgpu_p2p_destroy(c);
@@ -413,7 +583,7 @@ extern "C" cudaError_t kvd_mgpu_p2p_destroy(kvd_mgpu_p2p* c) {
 extern "C" cudaError_t kvd_mgpu_p2p_create_group(kvd_mgpu_p2p** ctxs, int nranks, const int* devices, int batch,
                                                  int num_q_heads, int head_dim) {
     using namespace kvd;
-    if (!ctxs || !devices || batch < 1 || num_q_heads < 1 || head_dim < 1 || (head_dim & 3) != 0 || nranks < 1 ||
+    if (!ctxs || !devices || batch < 1 || num_q_heads < 1 || head_dim < 1 || head_dim > kMaxDim || (head_dim & 3) != 0 || nranks < 1 ||
         nranks > kMaxRanks)
         return cudaErrorInvalidValue;
     for (int r = 0; r < nranks; ++r) ctxs[r] = nullptr;
@@ -421,7 +591,7 @@ extern "C" cudaError_t kvd_mgpu_p2p_create_group(kvd_mgpu_p2p** ctxs, int nranks
     cudaError_t e = cudaGetDevice(&prev);
     if (e != cudaSuccess) return e;
     const int rows = batch * num_q_heads;
-    int64_t ctas = (rows + kP2PRows - 1) / kP2PRows;
+    int64_t ctas = rows;
     // every rank runs the same grid: the co-resident bound of the smallest device
     for (int r = 0; r < nranks && e == cudaSuccess; ++r) {
         e = cudaSetDevice(devices[r]);
@@ -448,8 +618,6 @@ extern "C" cudaError_t kvd_mgpu_p2p_create_group(kvd_mgpu_p2p** ctxs, int nranks
             }
         }
     const size_t slab = static_cast<size_t>(rows) * (head_dim + 4);
-    const size_t gather_bytes = align256(2 * static_cast<size_t>(nranks) * slab * sizeof(float));
-    const size_t flag_bytes = align256(static_cast<size_t>(nranks) * ctas * sizeof(unsigned int));
     for (int r = 0; r < nranks && e == cudaSuccess; ++r) {
         e = cudaSetDevice(devices[r]);
         if (e != cudaSuccess) break;
@@ -461,7 +629,7 @@ extern "C" cudaError_t kvd_mgpu_p2p_create_group(kvd_mgpu_p2p** ctxs, int nranks
         c->rows = rows;
         c->ctas = static_cast<int>(ctas);
         c->slab_floats = slab;
-        c->region_bytes = gather_bytes + flag_bytes;
+        c->region_bytes = align256(2 * static_cast<size_t>(nranks) * slab * sizeof(unsigned long long));
         e = cudaMalloc(&c->region, c->region_bytes);
         if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c->epochs), c->ctas * sizeof(unsigned int));
         if (e == cudaSuccess) e = cudaMemset(c->region, 0, c->region_bytes);
@@ -470,8 +638,7 @@ extern "C" cudaError_t kvd_mgpu_p2p_create_group(kvd_mgpu_p2p** ctxs, int nranks
     }
     for (int r = 0; r < nranks && e == cudaSuccess; ++r)
         for (int q = 0; q < nranks; ++q) {
-            ctxs[r]->peers.gather[q] = static_cast<float*>(ctxs[q]->region);
-            ctxs[r]->peers.flags[q] = reinterpret_cast<unsigned int*>(static_cast<char*>(ctxs[q]->region) + gather_bytes);
+            ctxs[r]->peers.gather[q] = static_cast<unsigned long long*>(ctxs[q]->region);
         }
     if (e != cudaSuccess) {
         for (int r = 0; r < nranks; ++r)
@@ -514,7 +681,7 @@ extern "C" cudaError_t kvd_mgpu_p2p_reset(kvd_mgpu_p2p* c, cudaStream_t stream) 
     cudaError_t e = cudaDeviceSynchronize();
     // 2. none of any rank's (every rank is past step 1)
     if (e == cudaSuccess) e = p2p_barrier(c, stream);
-    // 3. epochs, flags and gather buffers back to their state at creation
+    // 3. epochs and gather buffers back to their state at creation
     if (e == cudaSuccess) e = cudaMemsetAsync(c->region, 0, c->region_bytes, stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(c->epochs, 0, c->ctas * sizeof(unsigned int), stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
@@ -523,9 +690,21 @@ extern "C" cudaError_t kvd_mgpu_p2p_reset(kvd_mgpu_p2p* c, cudaStream_t stream) 
     return e;
 }
 
+namespace {
+// Bytes of the tagged split records of a tensor-core decode of `r` (0 when
+// the decode cannot write them).
+size_t tagged_record_bytes(const kvd_decode_desc& r) {
+    const int P = kvd::gqa_tagged_splits(r);
+    return P > 0 ? kvd::align256(static_cast<size_t>(r.batch) * r.num_q_heads * P * (r.head_dim + 4) *
+                                 sizeof(unsigned long long))
+                 : 0;
+}
+}  // namespace
+
 extern "C" size_t kvd_mgpu_p2p_workspace_size(const kvd_decode_desc* desc) {
     if (!desc) return 0;
-    return kvd_mgpu_seq_split_workspace_size(desc, 1);
+    const size_t base = kvd_mgpu_seq_split_workspace_size(desc, 1);
+    return base ? base + tagged_record_bytes(record_desc(*desc)) : 0;
 }
 
 extern "C" cudaError_t kvd_mgpu_p2p_seq_split_decode(kvd_mgpu_p2p* c, const kvd_decode_desc* desc, const void* Q,
@@ -544,14 +723,20 @@ extern "C" cudaError_t kvd_mgpu_p2p_seq_split_decode(kvd_mgpu_p2p* c, const kvd_
     if (cudaGetDevice(&dev) != cudaSuccess || dev != c->device) return cudaErrorInvalidDevice;  // the rank's own GPU
     const kvd_decode_desc r = record_desc(*desc);
     const size_t rec = record_bytes(r);
+    // workspace: float records [rec] | (unused) [rec] | decode workspace | tagged records
+    const size_t base = kvd_mgpu_seq_split_workspace_size(desc, 1);
     char* ws = static_cast<char*>(workspace);
     float* local = reinterpret_cast<float*>(ws);
     char* dws = ws + 2 * rec;
-    const size_t dws_bytes = workspace_bytes - (dws - ws);
+    const size_t dws_bytes = base - 2 * rec;
     // 1. this rank's token range -> records. A dense tensor-core decode leaves
-    //    its split records in the workspace and the exchange kernel merges them,
-    //    so no separate combine launch runs.
-    SplitRecords splits{local, 1};
+    //    its split records in the workspace (tagged where it can) and the
+    //    exchange kernel merges them, so no separate combine launch runs.
+    SplitRecords splits{local, 1, nullptr, 0, c->epochs, false};
+    if (tagged_record_bytes(r) > 0) {
+        splits.tagged = reinterpret_cast<unsigned long long*>(ws + base);
+        splits.tagged_P = gqa_tagged_splits(r);
+    }
     cudaError_t e;
     int n = 0;
     if (!r.seq_lens && fast_path_ok(r, Q, K, V) && gqa_path_ok(r)) {
@@ -566,9 +751,10 @@ extern "C" cudaError_t kvd_mgpu_p2p_seq_split_decode(kvd_mgpu_p2p* c, const kvd_
         *launches = n;
         return e;
     }
-    // 2. merge, push, wait, merge: one kernel
-    // Programmatic dependent launch: the exchange's CTAs may be scheduled while the
-    // decode's last CTAs run and wait (griddepcontrol.wait) for its completion.
+    // 2. merge, push, wait, merge: one kernel, launched as a programmatic
+    // dependent so that its CTAs are resident while the decode runs. With
+    // tagged records they merge and push each row as soon as its records are
+    // there; otherwise they wait (griddepcontrol.wait) for the decode grid.
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(c->ctas), 1, 1);
     cfg.blockDim = dim3(kP2PThreads, 1, 1);
@@ -578,8 +764,9 @@ extern "C" cudaError_t kvd_mgpu_p2p_seq_split_decode(kvd_mgpu_p2p* c, const kvd_
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, p2p_exchange_combine_kernel, static_cast<const float*>(splits.partials), splits.P,
-                           c->peers, c->epochs, c->nranks, c->rank, c->rows, c->head_dim, c->heads, out,
+    e = cudaLaunchKernelEx(&cfg, p2p_exchange_combine_kernel, static_cast<const float*>(splits.partials),
+                           static_cast<const unsigned long long*>(splits.tagged_used ? splits.tagged : nullptr),
+                           splits.P, c->peers, c->epochs, c->nranks, c->rank, c->rows, c->head_dim, c->heads, out,
                            static_cast<int64_t>(desc->o_stride_b), static_cast<int64_t>(desc->o_stride_h),
                            static_cast<uint32_t>(desc->flags & (KVD_FLAG_OUT_BF16 | KVD_FLAG_OUT_F16)));
     if (e == cudaSuccess) ++n;
