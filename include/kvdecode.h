@@ -326,17 +326,22 @@ cudaError_t kvd_mgpu_seq_split_decode(const kvd_decode_desc* desc,
                                       void* comm, int nranks, cudaStream_t stream);
 
 /* The same sequence split with the record exchange done by the library's own
- * kernel over NVLink instead of NCCL: after the local decode, one kernel
- * merges this rank's split records of each row, stores the merged record
- * straight into every rank's gather buffer (CUDA IPC mappings of peer memory),
- * raises a flag per (rank, CTA) in each peer's memory, waits for all ranks'
- * flags (bounded: a rank that never arrives turns into KVD_STATUS_WAIT_TIMEOUT
- * after 2 s) and merges the gathered records. The exchange kernel never runs
- * more CTAs than fit on the GPU at once, so any batch size completes.
- * kvd_mgpu_p2p_create is collective (every rank calls it with the same sizes):
- * it allocates the exchange buffers (cudaMalloc) and swaps IPC handles once
- * over `comm`, which must outlive the context. Up to 8 ranks, head_dim a
- * multiple of 4. Every rank must make the same sequence of decode calls.
+ * kernel over NVLink instead of NCCL: one kernel merges this rank's split
+ * records of each row, stores the merged record straight into every rank's
+ * gather buffer (CUDA IPC mappings of peer memory) as 8-byte words that carry
+ * the call's epoch (so no fence or flag follows the stores), waits for every
+ * rank's record of its rows (bounded: a rank that never arrives turns into
+ * KVD_STATUS_WAIT_TIMEOUT after 2 s) and merges them into output rows. For a
+ * dense batch with up to 4 query heads per KV head and head_dim 128 the
+ * decode writes its split records in the same tagged form and the exchange
+ * kernel runs beside it, merging each row as soon as its records are there;
+ * otherwise it starts when the decode has completed. The exchange kernel
+ * never runs more CTAs than fit on the GPU at once, so any batch size
+ * completes. kvd_mgpu_p2p_create is collective (every rank calls it with the
+ * same sizes): it allocates the exchange buffers (cudaMalloc) and swaps IPC
+ * handles once over `comm`, which must outlive the context. Up to 8 ranks,
+ * head_dim a multiple of 4 and at most 256. Every rank must make the same
+ * sequence of decode calls.
  *
  * After a call that recorded KVD_STATUS_WAIT_TIMEOUT (a rank missed a call or
  * stalled), the rows of the timed-out CTAs are not written and the ranks' call
