@@ -181,7 +181,7 @@ constexpr int kP2PThreads = 128;  // 4 warps
 constexpr int kP2PWarps = kP2PThreads / 32;
 constexpr int kMaxRanks = 8;
 constexpr int kMaxMerge = 256;  // records merged per row (split count cap of the planner)
-constexpr int kMaxDim = 256;    // head_dim bound of the exchange
+constexpr int kMaxDim = 256;    // head_dim bound of the exchange (merged in passes of 128 dimensions)
 constexpr int kRecs = 4;        // records a thread holds at once (x 4 dimensions = 16 tagged words)
 
 struct P2PPeers {
@@ -234,11 +234,56 @@ __device__ __forceinline__ bool wait_word(const unsigned long long* p, unsigned 
     return true;
 }
 
+// About 4 KB: a CTA must fit in the shared memory that two CTAs of the
+// group-1 decode leave on an SM, so that it runs while they do.
 struct MergeSmem {
-    float ms[kMaxMerge], ls[kMaxMerge], wk[kMaxMerge];
-    float part[kP2PWarps][kMaxDim];
+    float ms[kMaxMerge];  // the records' maxima, then their weights
+    float ls[kMaxMerge];
+    float part[kP2PWarps][128];  // per-warp partial sums of one pass of 128 dimensions
     float red[kP2PWarps];
 };
+
+// Log-sum-exp weights of n records from their maxima sm.ms[k] and sums
+// sm.ls[k]: M = max_k ms[k], w_k = 2^(ms[k] - M) written over sm.ms[k], and
+// L = sum_k w_k ls[k], returned to every thread. Starts after a barrier that
+// made ms and ls complete; ends with one that makes the weights visible.
+__device__ __forceinline__ void lse_weights(int n, MergeSmem& sm, float& M, float& L) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    if (n <= 32) {  // few records: every thread reads them all
+        M = -INFINITY;
+        for (int k = 0; k < n; ++k) M = fmaxf(M, sm.ms[k]);
+        L = 0.f;
+        float mine = 0.f;
+        for (int k = 0; k < n; ++k) {
+            const float f = M == -INFINITY ? 0.f : exp2f(sm.ms[k] - M);
+            if (k == t) mine = f;
+            L = fmaf(f, sm.ls[k], L);
+        }
+        __syncthreads();  // every thread has read the maxima
+        if (t < n) sm.ms[t] = mine;
+        __syncthreads();
+        return;
+    }
+    float m = -INFINITY;
+    for (int k = t; k < n; k += blockDim.x) m = fmaxf(m, sm.ms[k]);
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (lane == 0) sm.red[warp] = m;
+    __syncthreads();
+    M = sm.red[0];
+    for (int w = 1; w < kP2PWarps; ++w) M = fmaxf(M, sm.red[w]);
+    float l = 0.f;
+    for (int k = t; k < n; k += blockDim.x) {  // each thread its own records only
+        const float f = M == -INFINITY ? 0.f : exp2f(sm.ms[k] - M);
+        sm.ms[k] = f;
+        l = fmaf(f, sm.ls[k], l);
+    }
+    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+    __syncthreads();  // every thread has read the maxima in red
+    if (lane == 0) sm.red[warp] = l;
+    __syncthreads();  // the sums are in red and the weights in ms
+    L = 0.f;
+    for (int w = 0; w < kP2PWarps; ++w) L += sm.red[w];
+}
 
 // One thread's share of a row of n tagged records (record k at first +
 // k * stride: m, l, 2 unused, o[D]): with_ml, m and l of records t, t + 128,
@@ -331,68 +376,40 @@ __device__ __forceinline__ bool merge_tagged(const unsigned long long* first, in
         ok = load_share(first, n, stride, g0, 0, true, e, sm, o, true, t0);
         if (!__syncthreads_and(ok)) return false;
     }
-    // weights: every thread from sm.ms / sm.ls (few records), or block-wide; kept in sm.wk
-    if (n <= 32) {
-        M = -INFINITY;
-        for (int k = 0; k < n; ++k) M = fmaxf(M, sm.ms[k]);
-        L = 0.f;
-        for (int k = 0; k < n; ++k) {
-            const float f = M == -INFINITY ? 0.f : exp2f(sm.ms[k] - M);
-            if (k == t) sm.wk[k] = f;
-            L = fmaf(f, sm.ls[k], L);
-        }
-        __syncthreads();  // sm.wk is complete
-    } else {
-        float m = -INFINITY;
-        for (int k = t; k < n; k += blockDim.x) m = fmaxf(m, sm.ms[k]);
-        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-        if (lane == 0) sm.red[warp] = m;
-        __syncthreads();
-        M = sm.red[0];
-        for (int w = 1; w < kP2PWarps; ++w) M = fmaxf(M, sm.red[w]);
-        float l = 0.f;
-        for (int k = t; k < n; k += blockDim.x) {
-            const float f = M == -INFINITY ? 0.f : exp2f(sm.ms[k] - M);
-            sm.wk[k] = f;
-            l = fmaf(f, sm.ls[k], l);
-        }
-        for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-        __syncthreads();  // every thread has read the maxima in red
-        if (lane == 0) sm.red[warp] = l;
-        __syncthreads();  // the sums are in red and the weights in wk
-        L = 0.f;
-        for (int w = 0; w < kP2PWarps; ++w) L += sm.red[w];
-    }
-    // this warp's partial sums over its records, dimension group by group
-    for (int g = lane; g < groups; g += 32) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int k0 = 0; k0 < n && ok; k0 += kP2PWarps * kRecs) {
-            // records not held from the first round: load again (waiting where a tag is not there yet)
-            if ((g != lane || k0 > 0) && !load_share(first, n, stride, g, k0, false, e, sm, o, true, t0)) {
-                ok = false;
-                break;
-            }
+    lse_weights(n, sm, M, L);
+    // per-warp partial sums over its records, in passes of 128 dimensions
+    for (int base = 0; base < D; base += 128) {
+        const int g = (base >> 2) + lane;  // this lane's dimension group in the pass
+        if (g < groups) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int k0 = 0; k0 < n && ok; k0 += kP2PWarps * kRecs) {
+                // records not held from the first round: load again (waiting where a tag is not there yet)
+                if ((base > 0 || k0 > 0) && !load_share(first, n, stride, g, k0, false, e, sm, o, true, t0)) {
+                    ok = false;
+                    break;
+                }
 #pragma unroll
-            for (int j = 0; j < kRecs; ++j) {
-                const int k = k0 + warp + kP2PWarps * j;
-                if (k < n) {
-                    const float f = sm.wk[k];
+                for (int j = 0; j < kRecs; ++j) {
+                    const int k = k0 + warp + kP2PWarps * j;
+                    if (k < n) {
+                        const float f = sm.ms[k];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) acc[i] = fmaf(f, o[j][i], acc[i]);
+                        for (int i = 0; i < 4; ++i) acc[i] = fmaf(f, o[j][i], acc[i]);
+                    }
                 }
             }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sm.part[warp][4 * lane + i] = acc[i];
         }
+        if (!__syncthreads_and(ok)) return false;
+        if (base + t < D) {
+            float O = 0.f;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) sm.part[warp][4 * g + i] = acc[i];
+            for (int w = 0; w < kP2PWarps; ++w) O += sm.part[w][t];
+            emit(base + t, O, L);
+        }
+        __syncthreads();  // sm is rewritten by the next pass or row
     }
-    if (!__syncthreads_and(ok)) return false;
-    for (int d = t; d < D; d += blockDim.x) {
-        float O = 0.f;
-#pragma unroll
-        for (int w = 0; w < kP2PWarps; ++w) O += sm.part[w][d];
-        emit(d, O, L);
-    }
-    __syncthreads();  // sm is rewritten by the next row
     return true;
 }
 
@@ -401,35 +418,17 @@ __device__ __forceinline__ bool merge_tagged(const unsigned long long* first, in
 template <class Emit>
 __device__ __forceinline__ void merge_float(const float* first, int n, size_t stride, int D, MergeSmem& sm, float& M,
                                             float& L, Emit emit) {
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int t = threadIdx.x;
     for (int k = t; k < n; k += blockDim.x) {
         sm.ms[k] = __ldcg(first + k * stride);
         sm.ls[k] = __ldcg(first + k * stride + 1);
     }
     __syncthreads();
-    float m = -INFINITY;
-    for (int k = t; k < n; k += blockDim.x) m = fmaxf(m, sm.ms[k]);
-    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    if (lane == 0) sm.red[warp] = m;
-    __syncthreads();
-    M = sm.red[0];
-    for (int w = 1; w < kP2PWarps; ++w) M = fmaxf(M, sm.red[w]);
-    float l = 0.f;
-    for (int k = t; k < n; k += blockDim.x) {
-        const float f = M == -INFINITY ? 0.f : exp2f(sm.ms[k] - M);
-        sm.wk[k] = f;
-        l = fmaf(f, sm.ls[k], l);
-    }
-    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-    __syncthreads();
-    if (lane == 0) sm.red[warp] = l;
-    __syncthreads();
-    L = 0.f;
-    for (int w = 0; w < kP2PWarps; ++w) L += sm.red[w];
+    lse_weights(n, sm, M, L);
     for (int d = t; d < D; d += blockDim.x) {
         float O = 0.f;
 #pragma unroll 8
-        for (int k = 0; k < n; ++k) O = fmaf(sm.wk[k], __ldcg(first + k * stride + 4 + d), O);
+        for (int k = 0; k < n; ++k) O = fmaf(sm.ms[k], __ldcg(first + k * stride + 4 + d), O);
         emit(d, O, L);
     }
     __syncthreads();  // sm is rewritten by the next row
@@ -437,10 +436,11 @@ __device__ __forceinline__ void merge_float(const float* first, int n, size_t st
 
 // Records of this rank: tagged (P per row, from a tagged decode that may still
 // be running) or float (src, P per row, from a completed decode grid).
-// At most 152 registers a thread (launched with kP2PThreads threads): a CTA
-// then fits on an SM beside two CTAs of the group-1 decode (120 registers a
-// thread after allocation rounding) and runs while they do.
-__global__ void __maxnreg__(152) p2p_exchange_combine_kernel(
+// At most 144 registers a thread (launched with kP2PThreads threads) and
+// about 4 KB of shared memory: a CTA then fits on an SM beside two CTAs of the
+// group-1 decode (120 registers a thread after allocation rounding, 2 x 95 KB
+// of shared memory) and runs while they do.
+__global__ void __maxnreg__(144) p2p_exchange_combine_kernel(
     const float* __restrict__ src, const unsigned long long* tagged, int P, const __grid_constant__ P2PPeers peers,
     unsigned int* epochs, int nranks, int rank, int rows, int D, int rows_per_b, void* out, int64_t o_sb,
     int64_t o_sh, uint32_t flags) {
