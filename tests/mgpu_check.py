@@ -119,7 +119,7 @@ def main() -> int:
                 shard = [torch.from_numpy(np.ascontiguousarray(a[:, :, lo:hi])).to(dev) for a in (K, V, ks, vs)]
                 ex = kvd.P2PExchange(comm, B, Hq, 128)
                 try:
-                    for step in range(5):  # several epochs: both buffer parities, flags counting up
+                    for step in range(5):  # several epochs: both buffer parities, epochs counting up
                         out = ex.decode(torch.from_numpy(q).to(dev), *shard, out_dtype=odt)
                         torch.cuda.synchronize()
                         o = out.float().cpu().numpy()
