@@ -78,7 +78,10 @@ struct GqaParams {
     // at tagged + ((b * Hq + hq) * P + split) * (D + 4), each word {value bits,
     // tag << 32} written with one 8-byte store, so a reader that sees the tag
     // sees the value and no fence or count is needed. tag = *tag_src + 1, read
-    // by every CTA before it allows its programmatic dependents to launch.
+    // by every CTA before it allows its programmatic dependents to launch. The
+    // grid is itself launched as a programmatic dependent of the previous
+    // exchange: its CTAs set up while that kernel ends and wait for it
+    // (griddepcontrol.wait) before any global memory access.
     // Compiled for groups up to kTagMaxGroup only (the larger groups' kernels
     // are at their register limit). nullptr: float records.
     unsigned long long* tagged;
@@ -985,7 +988,8 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV, QM>::THREADS, MINB) gqa_tc_k
     // CTAs retire; it waits for this grid's completion before reading its
     // output. With tagged records the dependent (the exchange) reads them while
     // this grid runs and moves the tag word on when it ends: every CTA reads
-    // the tag first and allows the dependents to launch only after that.
+    // the tag first and allows the dependents to launch only after that. (A
+    // dense batch: the item loop below reads no global memory before that.)
     bool tagged = false;
     if constexpr (G <= kTagMaxGroup) tagged = p.tagged != nullptr;
     if (!tagged) allow_dependents();
@@ -998,8 +1002,6 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV, QM>::THREADS, MINB) gqa_tc_k
     uint64_t* done = bars + C::B_DONE;
     uint64_t* drain = bars + C::B_DRAIN;
     if (threadIdx.x == 0) {
-        unsigned int tag = 0;
-        if (tagged) asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(tag) : "l"(p.tag_src) : "memory");
         for (int s = 0; s < NK; ++s) {
             mbar_init(&bars[C::B_KFULL + s], 1);       // producer arrive + transaction bytes
             mbar_init(&bars[C::B_KEMPTY + s], 1);      // QK commit
@@ -1021,12 +1023,22 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV, QM>::THREADS, MINB) gqa_tc_k
         mbar_init(drain, 1);
         *reinterpret_cast<int*>(smem + C::OFF_APPENDED) = 0;
         mbar_init(&bars[C::B_APPEND], EW);  // every epilogue warp, after its share of the fused append
-        if (tagged) *reinterpret_cast<unsigned int*>(smem + C::OFF_TAG) = tag + 1;
         fence_mbar_init();
     }
     if (warp == EW + 1) tmem_alloc(reinterpret_cast<uint32_t*>(smem + C::OFF_TMEM), C::TMEM_COLS);
     __syncthreads();
-    if (tagged) allow_dependents();  // every CTA of this grid has read the tag
+    if (tagged) {
+        // launched as a programmatic dependent of the previous exchange: wait for it (and its
+        // memory), read the tag it left, then let this call's exchange launch
+        grid_dependency_wait();
+        if (threadIdx.x == 0) {
+            unsigned int tag;
+            asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(tag) : "l"(p.tag_src) : "memory");
+            *reinterpret_cast<unsigned int*>(smem + C::OFF_TAG) = tag + 1;
+        }
+        __syncthreads();
+        allow_dependents();  // every CTA of this grid has read the tag
+    }
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + C::OFF_TMEM);
     if (warp == EW) {
@@ -1222,6 +1234,19 @@ cudaError_t launch_gqa_g(const CUtensorMap& km, const CUtensorMap& vm, const Gqa
         return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     });
     if (e != cudaSuccess) return e;
+    if (p.tagged) {  // a programmatic dependent of the previous exchange (see GqaParams::tagged)
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
+        cfg.blockDim = dim3(C::THREADS, 1, 1);
+        cfg.dynamicSmemBytes = C::SMEM_BYTES;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, kern, km, vm, p);
+    }
     kern<<<p.grid, C::THREADS, C::SMEM_BYTES, st>>>(km, vm, p);
     return cudaGetLastError();
 }

@@ -447,6 +447,9 @@ __global__ void __maxnreg__(144) p2p_exchange_combine_kernel(
     const int c = blockIdx.x, ctas = gridDim.x, t = threadIdx.x;
     const int rs = D + 4;
     __shared__ MergeSmem sm;
+    // The next call's tagged decode may launch now: it sets up beside this grid and
+    // waits for its completion before it touches global memory.
+    allow_dependents();
     if (!tagged) grid_dependency_wait();  // launched as a programmatic dependent: the float records are complete
     const unsigned int e = *reinterpret_cast<volatile unsigned int*>(epochs + c) + 1;
     const int par = static_cast<int>(e & 1u);
