@@ -22,7 +22,11 @@
  * before reading the decode's output. A caller's kernel launched after a
  * decode WITHOUT that attribute is ordered as usual; one launched WITH it must
  * itself wait (griddepcontrol.wait / cudaGridDependencySynchronize) before
- * reading the decode's output.
+ * reading the decode's output. In kvd_mgpu_p2p_seq_split_decode the decode
+ * is itself launched with the attribute (its CTAs set up while the kernel
+ * before it ends, and wait before any global memory access), and the
+ * record exchange lets the next kernel launch early: a caller's kernel that
+ * follows it with the attribute must wait in the same way.
  */
 #ifndef KVDECODE_H
 #define KVDECODE_H
