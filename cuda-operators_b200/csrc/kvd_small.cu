@@ -85,6 +85,10 @@ __global__ void __launch_bounds__(SmCfg<D>::THREADS) small_decode_kernel(const S
     float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
     float* rec = reinterpret_cast<float*>(smem + C::OFF_REC);
 
+    // Launched as a programmatic dependent of the kernel before it, and lets the
+    // next one launch at once: the CTAs set up while the previous grid ends and
+    // wait for it (griddepcontrol.wait) before touching global memory.
+    allow_dependents();
     // ---- one batch of bulk copies: K rows, V rows, both scale windows, the query row
     int koff = 0, voff = 0;
     if (tid == 0) {
@@ -92,6 +96,7 @@ __global__ void __launch_bounds__(SmCfg<D>::THREADS) small_decode_kernel(const S
         fence_mbar_init();
     }
     __syncthreads();
+    grid_dependency_wait();
     bool ok = true;
     if (n > 0) {
         const int64_t kv_off = b * p.kv_sb + hq * p.kv_sh + static_cast<int64_t>(t0) * D;
@@ -246,13 +251,15 @@ cudaError_t launch_small_d(const SmallParams& p, int cs, int heads, cudaStream_t
     cfg.blockDim = dim3(C::THREADS, 1, 1);
     cfg.dynamicSmemBytes = C::SMEM_BYTES;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = static_cast<unsigned>(cs);
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, small_decode_kernel<D>, p);
 }
 }  // namespace
