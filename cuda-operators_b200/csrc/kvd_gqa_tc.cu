@@ -992,7 +992,12 @@ __global__ void __launch_bounds__(GqaCfg<G, NK, NV, QM>::THREADS, MINB) gqa_tc_k
     // dense batch: the item loop below reads no global memory before that.)
     bool tagged = false;
     if constexpr (G <= kTagMaxGroup) tagged = p.tagged != nullptr;
-    if (!tagged) allow_dependents();
+    if (!tagged) {
+        // launched as a programmatic dependent of the kernel before it: wait for
+        // it (and its memory) before the first global access
+        grid_dependency_wait();
+        allow_dependents();
+    }
     if (next_item(p, blockIdx.x) >= p.n_items) {  // no (non-empty) item for this CTA (exiting allows the dependents)
         if (p.k_new) fused_append_finish(p);
         return;
@@ -1234,7 +1239,7 @@ cudaError_t launch_gqa_g(const CUtensorMap& km, const CUtensorMap& vm, const Gqa
         return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     });
     if (e != cudaSuccess) return e;
-    if (p.tagged) {  // a programmatic dependent of the previous exchange (see GqaParams::tagged)
+    {  // a programmatic dependent of the kernel before it (see gqa_tc_kernel)
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
         cfg.blockDim = dim3(C::THREADS, 1, 1);
@@ -1247,8 +1252,6 @@ cudaError_t launch_gqa_g(const CUtensorMap& km, const CUtensorMap& vm, const Gqa
         cfg.numAttrs = 1;
         return cudaLaunchKernelEx(&cfg, kern, km, vm, p);
     }
-    kern<<<p.grid, C::THREADS, C::SMEM_BYTES, st>>>(km, vm, p);
-    return cudaGetLastError();
 }
 
 }  // namespace

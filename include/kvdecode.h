@@ -22,11 +22,13 @@
  * before reading the decode's output. A caller's kernel launched after a
  * decode WITHOUT that attribute is ordered as usual; one launched WITH it must
  * itself wait (griddepcontrol.wait / cudaGridDependencySynchronize) before
- * reading the decode's output. In kvd_mgpu_p2p_seq_split_decode the decode
- * is itself launched with the attribute (its CTAs set up while the kernel
- * before it ends, and wait before any global memory access), and the
- * record exchange lets the next kernel launch early: a caller's kernel that
- * follows it with the attribute must wait in the same way.
+ * reading the decode's output. The head_dim-128 and small-problem decode
+ * kernels are themselves launched with the attribute: their CTAs may launch
+ * while the kernel before them on the stream ends, and wait
+ * (griddepcontrol.wait) before any global memory access, so they see
+ * everything that kernel wrote. The record exchange of
+ * kvd_mgpu_p2p_seq_split_decode lets the next kernel launch early too: a
+ * caller's kernel that follows it with the attribute must wait in the same way.
  */
 #ifndef KVDECODE_H
 #define KVDECODE_H
